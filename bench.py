@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""bench.py — decode+prefill tok/s of the int8 forward engine on the Llama-3-8B shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+One step is one batch of the workload through the engine's C ABI: `seqs` sequences per GPU (64) of `prompt` (512)
+seeded random prompt tokens, prefilled in blocks (b200fwd_run), then `gen` (256) greedy tokens each on the device
+(b200fwd_generate_greedy). Weights: N(0, 0.02), quantized to int8 with one float32 scale per group of 32, made on the
+device (8.4 GB; far larger than L2, so every step reads them from HBM). Sequences are sharded across GPUs with no
+collective on the data path (each rank its own 64: weak scaling); ranks meet only at the timing barrier.
+
+value: tokens (prompt + generated, all ranks) / the device time of the step's engine calls (CUDA events on the
+engine's stream, max over ranks). e2e: the same through the host-buffer calls, by the host clock around each step,
+host-to-device copies of the prompts and device-to-host reads of the generated ids inside. roofline: the dominant
+kernel (the int8 matmul) timed alone at the decode step's shapes with CUDA events, algorithmic bytes over its
+duration against the measured HBM copy bandwidth. cpu_baseline: the oracle (a C++ restatement of the reference's
+WASM-SIMD path, every host thread) on a bounded sample of the same workload.
+
+--impl reference: the reference's CPU path on this host (the oracle port: the reference's AssemblyScript kernels
+cannot be built or run here), every host thread, one sequence of the same model per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "pyodide-llm_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode+prefill tok/s, 8B-shape int8 (64 seq x (512 prompt + 256 greedy) per GPU)"
+HEADER = (4096, 14336, 32, 32, 8, -128256, 8192)
+THETA = 500000.0
+BOS = 1
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--seqs", type=int, default=64)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--gen", type=int, default=256)
+    p.add_argument("--block", type=int, default=64, help="prompt positions per prefill call")
+    p.add_argument("--cpu-prompt", type=int, default=16)
+    p.add_argument("--cpu-gen", type=int, default=8)
+    p.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "stories15m"])
+    return p.parse_args()
+
+
+def model_of(args):
+    if args.model == "stories15m":
+        return (288, 768, 6, 6, 6, 32000, 256), 10000.0
+    return HEADER, THETA
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+class Clocks:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = str(index), [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", self.index], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def cpu_sample(ckpt_host, plan, args, threads):
+    """The oracle on one sequence: cpu_prompt prompt tokens (one block) then cpu_gen greedy steps. tok/s."""
+    import oracle
+
+    t0 = time.perf_counter()
+    eng = oracle.OracleEngine(ckpt_host, plan, half_keys=1, threads=threads)
+    setup = time.perf_counter() - t0
+    rng = np.random.default_rng(7)
+    vocab = abs(HEADER[5]) if args.model == "llama3-8b" else 32000
+    prompt = [BOS] + [int(t) for t in rng.integers(0, vocab, args.cpu_prompt - 1)]
+    t0 = time.perf_counter()
+    eng.forward_many(prompt[:-1], 0)
+    token = prompt[-1]
+    for s in range(args.cpu_gen):
+        token = int(np.argmax(eng.forward(token, len(prompt) - 1 + s)))
+    dt = time.perf_counter() - t0
+    eng.close()
+    return (args.cpu_prompt + args.cpu_gen) / dt, dt, setup
+
+
+def reference_arm(args):
+    """bench.py --impl reference: the oracle port of the reference's CPU path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    from b200fwd import synthetic
+
+    header, theta = model_of(args)
+    torch.set_num_threads(host_threads())
+    file = synthetic.make(header, seed=0, device="cpu")
+    plan = synthetic.plan_for(header, file, theta)
+    ckpt = file.numpy()
+    threads = host_threads()
+    times = []
+    for i in range(args.warmup + args.steps):
+        v, dt, _ = cpu_sample(ckpt, plan, args, threads)
+        if i >= args.warmup:
+            times.append(dt)
+    per = float(np.mean(times))
+    value = (args.cpu_prompt + args.cpu_gen) / per
+    sample = (f"1 sequence per step: {args.cpu_prompt} prompt tokens in one block + {args.cpu_gen} greedy steps, "
+              f"the whole {args.model} int8 model")
+    out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+           "config": {"workload": f"{args.model} int8, {sample}", "model": args.model},
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+           "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference's AssemblyScript/WASM kernels cannot be built here (no node, no asc); the oracle "
+                   "is their C++ restatement, pinned to the reference's bit-exact checks"}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def matmul_roofline(lib, M, stream, peaks, reps=12):
+    """The int8 matmul alone at the decode step's shapes: every matrix of a layer (q, k, v, o, w1, w3, w2) at M
+    tokens, cycling over 8 distinct layers' worth of weights (2 GB, beyond L2). CUDA events on the stream."""
+    import torch
+
+    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+    layers = 8
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    mats = []
+    for rows, n in shapes:
+        w = torch.randint(-127, 128, (layers, rows, n), dtype=torch.int8, device="cuda", generator=g)
+        s = torch.rand((layers, rows, n // 32), device="cuda", generator=g) * 0.019 + 0.001
+        mats.append((w, s, rows, n))
+    nmax = 14336
+    xq = torch.randint(1, 128, (M, nmax), dtype=torch.int8, device="cuda", generator=g)
+    xs = torch.rand((M, nmax // 32), device="cuda", generator=g) * 0.1
+    out = torch.empty((M, 14336), device="cuda")
+    st = torch.cuda.ExternalStream(stream)
+    import ctypes
+
+    def launch(i):
+        w, s, rows, n = mats[i % len(mats)]
+        layer = (i // len(mats)) % layers
+        rc = lib.b200k_matmul_q8r(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(xq.data_ptr()),
+                                  ctypes.c_void_p(xs.data_ptr()), ctypes.c_void_p(w[layer].data_ptr()),
+                                  ctypes.c_void_p(s[layer].data_ptr()), None, n, 0, rows, M, 14336, nmax, nmax // 32,
+                                  ctypes.c_void_p(stream))
+        assert rc == 0
+        return rows * n * (1 + 4 / 32) + M * n * (1 + 4 / 32) + M * rows * 4
+
+    for i in range(len(mats) * 2):
+        launch(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    count = len(mats) * reps
+    total = 0.0
+    start.record(st)
+    for i in range(count):
+        total += launch(i)
+    end.record(st)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    per_launch_bytes = total / count
+    per_launch_s = ms / 1e3 / count
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    peak = float(peaks["hbm_gbs"])
+    del mats
+    torch.cuda.empty_cache()
+    return {"kernel": "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": None, "M": M, "per_launch_us": per_launch_s * 1e6,
+            "algorithmic_bytes_per_launch": per_launch_bytes}
+
+
+def b200_arm(args):
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from b200fwd import abi, synthetic
+    from b200fwd.forward import Engine
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    header, theta = model_of(args)
+    vocab = abs(header[5])
+    S, P, G = args.seqs, args.prompt, args.gen
+    file = synthetic.make(header, seed=0, device="cuda")
+    plan = synthetic.plan_for(header, file, theta)
+    ckpt_host = file.cpu().numpy() if rank == 0 else None
+    eng = Engine(file.data_ptr(), plan, checkpoint_on_device=True, size=file.numel(), half_keys=True, slots=S,
+                 max_tokens=S * args.block, capacity=P + G, device=local)
+    del file
+    torch.cuda.empty_cache()
+    rng = np.random.default_rng(1000 + rank)
+    prompts = rng.integers(0, vocab, size=(S, P), dtype=np.int32)
+    prompts[:, 0] = BOS
+    stream = eng.stream()
+    st = torch.cuda.ExternalStream(stream)
+    slots_all = np.arange(S, dtype=np.int32)
+
+    def step(events=None):
+        """one batch: prefill positions 0..P-2 in blocks, then G greedy steps from the last prompt token"""
+        for b0 in range(0, P - 1, args.block):
+            n = min(args.block, P - 1 - b0)
+            sl = np.repeat(slots_all, n)
+            tk = prompts[:, b0:b0 + n].reshape(-1)
+            ps = np.tile(np.arange(b0, b0 + n, dtype=np.int32), S)
+            if events is not None:
+                events.append(torch.cuda.Event(enable_timing=True))
+                events[-1].record(st)
+            eng.run(sl, tk, ps)
+            if events is not None:
+                events.append(torch.cuda.Event(enable_timing=True))
+                events[-1].record(st)
+        if events is not None:
+            events.append(torch.cuda.Event(enable_timing=True))
+            events[-1].record(st)
+        ids = eng.generate_greedy(slots_all, prompts[:, P - 1], np.full(S, P - 1, np.int32), G)
+        if events is not None:
+            events.append(torch.cuda.Event(enable_timing=True))
+            events[-1].record(st)
+        return ids
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    launches0 = eng.launch_count()
+    wall, device_ms, prefill_ms, decode_ms = [], [], [], []
+    with Clocks(local) as clocks:
+        for _ in range(args.steps):
+            ev = []
+            t0 = time.perf_counter()
+            step(ev)
+            torch.cuda.synchronize()
+            wall.append(time.perf_counter() - t0)
+            pairs = [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)]
+            prefill_ms.append(sum(pairs[:-1]))
+            decode_ms.append(pairs[-1])
+            device_ms.append(sum(pairs))
+    barrier()
+    launches = eng.launch_count() - launches0
+
+    def worst(x):
+        t = torch.tensor([float(x)], device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_step = worst(np.mean(device_ms))
+    wall_step = worst(np.mean(wall))
+    pre = worst(np.mean(prefill_ms))
+    dec = worst(np.mean(decode_ms))
+    tokens = S * (P + G) * world
+    result = None
+    if rank == 0:
+        peaks, which = measured_peaks()
+        roof = matmul_roofline(abi.load(), S, stream, peaks)
+        roof["peak_source"] = which
+        cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
+        del ckpt_host
+        # each engine call copies its token table (4 x max_tokens int32) from pinned memory; greedy 2 more words
+        runs = -(-(P - 1) // args.block)
+        h2d = (runs + 1) * 16 * S * args.block + 8
+        d2h = S * G * 4 + 4  # the generated ids and the not-finite flag
+        clk = clocks.summary()
+        result = {
+            "metric": METRIC, "value": tokens / (ms_step / 1e3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{args.model} int8 end to end: {S} sequences per GPU x ({P} prompt tokens "
+                                   f"prefilled in blocks of {args.block} + {G} greedy tokens), sharded by sequence",
+                       "model": args.model, "global_batch": S * world, "seq_len": P + G, "prompt": P,
+                       "generated": G, "parallelism": f"dp{world} (independent sequences)", "kv": "float16",
+                       "activations": "7-bit + bias 64 (relaxed)", "float_order": "exact (the reference's)",
+                       "l2": "inputs larger than L2: 8.4 GB of weights read per step"},
+            "prefill_tok_s": S * (P - 1) * world / (pre / 1e3), "decode_tok_s": S * G * world / (dec / 1e3),
+            "e2e": {"value": tokens / wall_step, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": roof,
+            "cpu_baseline": {"value": cpu_v, "unit": "tok/s", "cores": host_threads(), "kind": "port",
+                             "sample": f"1 sequence: {args.cpu_prompt} prompt tokens (one block) + {args.cpu_gen} "
+                                       f"greedy steps of the same model ({cpu_dt:.1f} s)"},
+            "gpu_launches": launches // max(1, args.steps) * args.steps,
+            "clocks": clk,
+        }
+    eng.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

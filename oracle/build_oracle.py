@@ -1,7 +1,7 @@
 """TEST INFRASTRUCTURE: builds the oracle (oracle.cpp, a C++ restatement of the reference's CPU path) into
 oracle/liboracle.so. Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline load it.
 
-    python oracle/build.py
+    python oracle/build_oracle.py
 
 -ffp-contract=off keeps every multiply and add rounded on its own, as WASM's f32 operations are. x86-64-v2 keeps
 the library runnable on any x86-64 host the GPU boxes have (the build runs in one container, the tests in another).

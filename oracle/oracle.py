@@ -23,9 +23,9 @@ _lib = None
 def load():
     global _lib
     if _lib is None:
-        from build import build  # oracle/build.py
-
         sys.path.insert(0, str(HERE))
+        from build_oracle import build
+
         path = build()
         lib = ctypes.CDLL(str(path))
         P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64

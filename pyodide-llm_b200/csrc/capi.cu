@@ -1,0 +1,134 @@
+// capi.cu — the kernel entry points of include/b200fwd.h (b200k_*): the exports of kernels/kernel.ts and
+// kernels/kernel_relaxed.ts (public/jobs.js:56-62 lists them), as sm_100a kernels on device pointers.
+#include <string>
+
+#include "common.h"
+#include "kernels.h"
+
+using namespace b200;
+
+namespace {
+
+template <typename F>
+int guarded(F &&f) {
+  try {
+    return f();
+  } catch (...) {
+    return fail(B200FWD_EINVAL, "exception in a kernel entry");
+  }
+}
+
+int matmul(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, const int32_t *wc,
+           int32_t n, int32_t r0, int32_t r1, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
+           bool relaxed, b200fwd_stream stream) {
+  if (!xout || !xq || !xs || !wq || !ws) return fail(B200FWD_EINVAL, "matmul: null pointer");
+  if (n <= 0 || n % 32) return fail(B200FWD_EINVAL, "matmul: n must be whole groups of 32");
+  if (r0 < 0 || r1 < r0 || count < 1) return fail(B200FWD_EINVAL, "matmul: bad rows or count");
+  if (r1 == r0) return 0;
+  if (q_stride % 16 || (reinterpret_cast<uintptr_t>(xq) % 16) || (reinterpret_cast<uintptr_t>(wq) % 16))
+    return fail(B200FWD_EINVAL, "matmul: weights and activations must be 16-byte aligned (16-byte loads)");
+  MatJobs jobs{};
+  const int ng = n / 32;
+  jobs.job[0] = {wq + (int64_t)r0 * n, ws + (int64_t)r0 * ng, wc ? wc + (int64_t)r0 * ng : nullptr, xout + r0, r1 - r0,
+                 0, out_stride};
+  jobs.njobs = 1;
+  jobs.n = n;
+  jobs.total_rows = r1 - r0;
+  return launch_matvec(jobs, xq, xs, q_stride, s_stride, count, relaxed, as_stream(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200k_quantize_x(int8_t *xq, float *xs, const float *x, int32_t n, int32_t bias, int32_t count, int64_t x_stride,
+                     int64_t q_stride, int64_t s_stride, b200fwd_stream stream) {
+  return guarded([&] {
+    if (bias != 0 && bias != 64) return fail(B200FWD_EINVAL, "quantize_x: bias must be 0 or 64");
+    return launch_quantize(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride, as_stream(stream));
+  });
+}
+
+int b200k_int8_sums(int32_t *out, const int8_t *w, int64_t groups, b200fwd_stream stream) {
+  return guarded([&] { return launch_int8_sums(out, w, groups, as_stream(stream)); });
+}
+
+int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                     const int32_t *wc, int32_t n, int32_t r0, int32_t r1, int32_t count, int64_t out_stride,
+                     int64_t q_stride, int64_t s_stride, b200fwd_stream stream) {
+  return guarded([&] {
+    return matmul(xout, xq, xs, wq, ws, wc, n, r0, r1, count, out_stride, q_stride, s_stride, true, stream);
+  });
+}
+
+int b200k_matmul_q8(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
+                    int32_t r0, int32_t r1, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
+                    b200fwd_stream stream) {
+  return guarded([&] {
+    return matmul(xout, xq, xs, wq, ws, nullptr, n, r0, r1, count, out_stride, q_stride, s_stride, false, stream);
+  });
+}
+
+int b200k_rmsnorm(float *out, const float *x, const float *w, int32_t n, float eps, int32_t count, int64_t stride,
+                  b200fwd_stream stream) {
+  return guarded([&] { return launch_rmsnorm(out, x, w, n, eps, count, stride, as_stream(stream)); });
+}
+
+int b200k_rope(float *v, const float *fcr, const float *fci, int32_t nh, int32_t hs, int32_t rot,
+               b200fwd_stream stream) {
+  return guarded([&] {
+    if (hs % 2) return fail(B200FWD_EINVAL, "rope: the head size must be even");
+    return launch_rope(v, fcr, fci, nh, hs, rot, as_stream(stream));
+  });
+}
+
+int b200k_attention(float *out, const float *q, const void *kc, const void *vc, float *att, int32_t pos, int32_t nh,
+                    int32_t nkv, int32_t hs, int32_t h0, int32_t h1, int32_t half, b200fwd_stream stream) {
+  return guarded([&] {
+    if (pos < 0 || nh < 1 || nkv < 1 || nh % nkv || hs < 1 || h0 < 0 || h1 > nh || h0 > h1)
+      return fail(B200FWD_EINVAL, "attention: bad sizes");
+    if (h0 == h1) return 0;
+    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, nullptr, nullptr, pos, 1, 0, pos + 1, pos + 1, nh,
+                            nkv, hs, h0, h1, half ? 1 : 0, as_stream(stream));
+  });
+}
+
+int b200k_attention_batch(float *out, const float *q, const void *kc, const void *vc, float *att, const int32_t *seq,
+                          const int32_t *pos, int32_t n, int64_t seq_stride, int32_t scratch_positions, int32_t nh,
+                          int32_t nkv, int32_t hs, int32_t half, b200fwd_stream stream) {
+  return guarded([&] {
+    if (!seq || !pos || n < 0 || nh < 1 || nkv < 1 || nh % nkv || scratch_positions < 1)
+      return fail(B200FWD_EINVAL, "attention_batch: bad arguments");
+    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, seq, pos, 0, n, seq_stride, scratch_positions,
+                            scratch_positions, nh, nkv, hs, 0, nh, half ? 1 : 0, as_stream(stream));
+  });
+}
+
+int b200k_to_f16(uint16_t *out, const float *x, int64_t n, b200fwd_stream stream) {
+  return guarded([&] { return launch_to_f16(out, x, n, as_stream(stream)); });
+}
+
+int b200k_from_f16(float *out, const uint16_t *x, int64_t n, b200fwd_stream stream) {
+  return guarded([&] { return launch_from_f16(out, x, n, as_stream(stream)); });
+}
+
+int b200k_swiglu(float *out, const float *h1, const float *h3, int64_t n, b200fwd_stream stream) {
+  return guarded([&] { return launch_swiglu(out, h1, h3, n, as_stream(stream)); });
+}
+
+int b200k_add_inplace(float *x, const float *y, int64_t n, b200fwd_stream stream) {
+  return guarded([&] { return launch_add_inplace(x, y, n, as_stream(stream)); });
+}
+
+int b200k_add_columns(float *y, const float *rows, const float *a, int32_t count, int32_t n, b200fwd_stream stream) {
+  return guarded([&] { return launch_add_columns(y, n, rows, a, count, count, n, 1, as_stream(stream)); });
+}
+
+int b200k_argmax(int32_t *out, const float *x, int32_t n, b200fwd_stream stream) {
+  return guarded([&] {
+    if (n < 1) return fail(B200FWD_EINVAL, "argmax: no values");
+    return launch_argmax(out, x, n, n, 1, 0, as_stream(stream));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,685 @@
+// engine.cu — the forward engine of include/b200fwd.h: what public/forward.js createForward() is to
+// llama2_numpy.Llama(external=...), on one B200.
+//
+// HBM layout:
+//  - each int8 matrix in its own 256-byte-aligned block: values [layers][rows][n], then scales [layers][rows][n/32]
+//    (the checkpoint's order, moved off the file's unaligned offsets so that rows load as 16-byte vectors);
+//  - the norm weights and the RoPE tables as float32;
+//  - the KV cache of every slot: [slot][layer][keys|values][capacity][kvDim] in float16 or float32, the layout of
+//    forward.js:269-273 per slot, its capacity doubled as forward.js grow() does (forward.js:274-289);
+//  - the activations of up to max_tokens tokens, one row each (forward.js keeps them a frame apart, :192-208).
+// run() is forward.js run() (forward.js:452-531) over tokens that may belong to different slots.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "kernels.h"
+
+namespace b200 {
+
+std::atomic<uint64_t> launches{0};
+
+std::string &last_error() {
+  thread_local std::string message;
+  return message;
+}
+
+int fail(int code, const std::string &message) {
+  last_error() = message;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(e == cudaErrorMemoryAllocation ? B200FWD_ENOMEM : B200FWD_ECUDA,
+              std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+namespace {
+
+struct Matrix {
+  int8_t *w = nullptr;
+  float *s = nullptr;
+  int rows = 0, n = 0, layers = 1;
+  const int8_t *layer_w(int l) const { return w + (int64_t)l * rows * n; }
+  const float *layer_s(int l) const { return s + (int64_t)l * rows * (n / 32); }
+};
+
+// kernel.ts:383-392 half on the host, for keysAndValues
+float half_bits_to_float(uint16_t h) {
+  const int32_t v = (int32_t)(int16_t)h;
+  uint32_t u = (uint32_t)((v << 13) & (int32_t)0x8fffffff);
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f * 5.192296858534828e33f;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+struct b200fwd_engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  b200fwd_plan plan{};
+  int dim, hidden, layers, heads, kvHeads, hs, vocab, seqLen, kvDim, qDim, XQ;
+  bool relaxed, half;
+  int bias;
+  float eps;
+  Matrix emb, wq, wk, wv, wo, w1, w2, w3, wcls;
+  float *attW = nullptr, *ffnW = nullptr, *finalW = nullptr, *cosT = nullptr, *sinT = nullptr;
+  int nch = 0;
+  int32_t *channels = nullptr;
+  float *columns = nullptr;
+  // the cache
+  int slots = 1, capacity = 0;
+  uint8_t *cache = nullptr;
+  // activations
+  int T = 0;
+  float *x = nullptr, *xb = nullptr, *q = nullptr, *kn = nullptr, *vn = nullptr, *hb = nullptr, *hb2 = nullptr;
+  float *att = nullptr;
+  int8_t *xq = nullptr;
+  float *xs = nullptr;
+  float *xl = nullptr, *picked = nullptr, *logits = nullptr;
+  int logit_rows = 0;
+  int32_t *argmax = nullptr;
+  int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad
+  int32_t *meta_h = nullptr;    // pinned host copy
+  int32_t *history = nullptr;   // greedy ids [slots][steps]
+  int history_len = 0;
+  float *bound = nullptr;       // Python's logits array (host)
+  std::vector<float> last_logits;
+  uint64_t bytes = 0;
+  std::vector<void *> allocations;
+  uint64_t launches_at_create = 0;
+  std::string backend;
+
+  int32_t *tokens_d() { return meta; }
+  int32_t *seq_d() { return meta + T; }
+  int32_t *pos_d() { return meta + 2 * T; }
+  int32_t *want_d() { return meta + 3 * T; }
+  int32_t *step_d() { return meta + 4 * T; }
+  int32_t *bad_d() { return meta + 4 * T + 1; }
+  int esize() const { return half ? 2 : 4; }
+  int64_t seq_stride() const { return (int64_t)layers * 2 * capacity * kvDim; }
+  uint8_t *layer_keys(int l) { return cache + (int64_t)(l * 2) * capacity * kvDim * esize(); }
+  uint8_t *layer_values(int l) { return cache + (int64_t)(l * 2 + 1) * capacity * kvDim * esize(); }
+};
+
+namespace {
+
+int alloc(b200fwd_engine *e, void **p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  cudaError_t err = cudaMalloc(p, bytes);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMalloc");
+  e->allocations.push_back(*p);
+  e->bytes += bytes;
+  return 0;
+}
+
+void release(b200fwd_engine *e, void *p, size_t bytes) {
+  if (!p) return;
+  cudaFree(p);
+  auto it = std::find(e->allocations.begin(), e->allocations.end(), p);
+  if (it != e->allocations.end()) e->allocations.erase(it);
+  e->bytes -= bytes;
+}
+
+#define CHECK(expr)              \
+  do {                           \
+    int rc_ = (expr);            \
+    if (rc_) return rc_;         \
+  } while (0)
+
+int64_t elements(const b200fwd_tensor &t) {
+  int64_t c = 1;
+  for (int i = 0; i < t.ndim; i++) c *= t.shape[i];
+  return c;
+}
+
+cudaMemcpyKind copy_kind(bool on_device) { return on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice; }
+
+int upload_matrix(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_device, const b200fwd_tensor &t,
+                  const char *name, Matrix &m) {
+  if (t.kind != B200FWD_TENSOR_INT8)
+    return fail(B200FWD_EUNSUPPORTED, std::string("tensor ") + name + " is not int8 (this engine runs int8 only)");
+  if (t.ndim < 2 || t.ndim > 3) return fail(B200FWD_EINVAL, std::string("tensor ") + name + " has a bad shape");
+  m.rows = (int)t.shape[t.ndim - 2];
+  m.n = (int)t.shape[t.ndim - 1];
+  m.layers = t.ndim == 3 ? (int)t.shape[0] : 1;
+  if (t.group != 32 || m.n % 32)
+    return fail(B200FWD_EUNSUPPORTED, std::string("tensor ") + name + ": the int8 kernels take groups of 32");
+  const int64_t count = elements(t);
+  if (t.offset < 0 || t.scales < 0 || (size_t)(t.offset + count) > size || (size_t)(t.scales + count / 8) > size)
+    return fail(B200FWD_EINVAL, std::string("tensor ") + name + " lies outside the checkpoint");
+  CHECK(alloc(e, (void **)&m.w, count));
+  CHECK(alloc(e, (void **)&m.s, count / 32 * 4));
+  B200_CUDA(cudaMemcpyAsync(m.w, ckpt + t.offset, count, copy_kind(on_device), e->stream));
+  B200_CUDA(cudaMemcpyAsync(m.s, ckpt + t.scales, count / 32 * 4, copy_kind(on_device), e->stream));
+  return 0;
+}
+
+int upload_floats(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_device, const b200fwd_tensor &t,
+                  const char *name, int64_t want, float **out) {
+  if (t.kind != B200FWD_TENSOR_F32)
+    return fail(B200FWD_EUNSUPPORTED, std::string("tensor ") + name + " is not float32");
+  const int64_t count = elements(t);
+  if (count != want) return fail(B200FWD_EINVAL, std::string("tensor ") + name + " has the wrong size");
+  if (t.offset < 0 || (size_t)(t.offset + 4 * count) > size)
+    return fail(B200FWD_EINVAL, std::string("tensor ") + name + " lies outside the checkpoint");
+  CHECK(alloc(e, (void **)out, count * 4));
+  B200_CUDA(cudaMemcpyAsync(*out, ckpt + t.offset, count * 4, copy_kind(on_device), e->stream));
+  return 0;
+}
+
+// the activations and scratch of T tokens against a cache of `capacity` positions
+int alloc_activations(b200fwd_engine *e) {
+  const int T = e->T;
+  CHECK(alloc(e, (void **)&e->x, (size_t)T * e->dim * 4));
+  CHECK(alloc(e, (void **)&e->xb, (size_t)T * e->qDim * 4));
+  CHECK(alloc(e, (void **)&e->q, (size_t)T * e->qDim * 4));
+  CHECK(alloc(e, (void **)&e->kn, (size_t)T * e->kvDim * 4));
+  CHECK(alloc(e, (void **)&e->vn, (size_t)T * e->kvDim * 4));
+  CHECK(alloc(e, (void **)&e->hb, (size_t)T * e->hidden * 4));
+  CHECK(alloc(e, (void **)&e->hb2, (size_t)T * e->hidden * 4));
+  CHECK(alloc(e, (void **)&e->xq, (size_t)T * e->XQ));
+  CHECK(alloc(e, (void **)&e->xs, (size_t)T * (e->XQ / 32) * 4));
+  CHECK(alloc(e, (void **)&e->xl, (size_t)T * e->dim * 4));
+  CHECK(alloc(e, (void **)&e->picked, (size_t)T * std::max(1, e->nch) * 4));
+  CHECK(alloc(e, (void **)&e->argmax, (size_t)T * 4));
+  CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 2) * 4));
+  B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 2) * 4, e->stream));
+  B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 2) * 4));
+  return 0;
+}
+
+int ensure_logit_rows(b200fwd_engine *e, int rows) {
+  if (rows <= e->logit_rows) return 0;
+  B200_CUDA(cudaStreamSynchronize(e->stream));
+  release(e, e->logits, (size_t)e->logit_rows * e->vocab * 4);
+  e->logits = nullptr;
+  const int want = std::max(rows, std::min(e->T, e->slots));
+  CHECK(alloc(e, (void **)&e->logits, (size_t)want * e->vocab * 4));
+  e->logit_rows = want;
+  return 0;
+}
+
+// forward.js:274-289 grow: the capacity doubled (at least to pos + 1, at most seq_len), every slot's keys and values
+// copied to the larger blocks (their values do not change)
+int grow(b200fwd_engine *e, int pos) {
+  const int larger = std::min(std::max(2 * e->capacity, pos + 1), e->seqLen);
+  if (larger <= e->capacity) return 0;
+  const size_t old_block = (size_t)e->capacity * e->kvDim * e->esize();
+  const size_t new_block = (size_t)larger * e->kvDim * e->esize();
+  const size_t blocks = (size_t)e->slots * e->layers * 2;
+  uint8_t *cache = nullptr;
+  CHECK(alloc(e, (void **)&cache, blocks * new_block));
+  if (e->cache && e->capacity > 0)
+    B200_CUDA(cudaMemcpy2DAsync(cache, new_block, e->cache, old_block, old_block, blocks, cudaMemcpyDeviceToDevice,
+                                e->stream));
+  B200_CUDA(cudaStreamSynchronize(e->stream));
+  release(e, e->cache, blocks * old_block);
+  release(e, e->att, (size_t)e->T * e->heads * e->capacity * 4);
+  e->cache = cache;
+  e->capacity = larger;
+  e->att = nullptr;
+  CHECK(alloc(e, (void **)&e->att, (size_t)e->T * e->heads * e->capacity * 4));
+  return 0;
+}
+
+// the layers over n tokens whose ids, slots and positions are in meta (device); the logits of the `want` tokens
+// (their indices in want_d) into logits rows 0..want-1, and their argmax. Enqueues only (graph-capturable).
+int forward_device(b200fwd_engine *e, int n, int want, int max_count) {
+  cudaStream_t st = e->stream;
+  const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32;
+  CHECK(launch_embed(e->emb.w, e->emb.s, 32, e->tokens_d(), n, D, e->x, D, st));
+  for (int l = 0; l < e->layers; l++) {
+    CHECK(launch_norm_quantize(e->x, D, e->attW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
+                               nullptr, 0, nullptr, nullptr, 0, st));
+    MatJobs qkv{};
+    qkv.job[0] = {e->wq.layer_w(l), e->wq.layer_s(l), nullptr, e->q, e->wq.rows, 0, QD};
+    qkv.job[1] = {e->wk.layer_w(l), e->wk.layer_s(l), nullptr, e->kn, e->wk.rows, 0, KVD};
+    qkv.job[2] = {e->wv.layer_w(l), e->wv.layer_s(l), nullptr, e->vn, e->wv.rows, 0, KVD};
+    qkv.njobs = 3;
+    qkv.n = D;
+    qkv.total_rows = e->wq.rows + e->wk.rows + e->wv.rows;
+    CHECK(launch_matvec(qkv, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+    CHECK(launch_rope_cache(e->q, QD, e->kn, e->vn, KVD, e->cosT, e->sinT, e->pos_d(), e->seq_d(), n,
+                            e->layer_keys(l), e->layer_values(l), e->seq_stride(), e->half ? 1 : 0, e->heads,
+                            e->kvHeads, e->hs, e->plan.rotary, st));
+    CHECK(launch_attention(e->xb, QD, e->q, QD, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(),
+                           0, n, e->seq_stride(), e->capacity, max_count, e->heads, e->kvHeads, e->hs, 0, e->heads,
+                           e->half ? 1 : 0, st));
+    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, XS, st));
+    MatJobs o{};
+    o.job[0] = {e->wo.layer_w(l), e->wo.layer_s(l), nullptr, e->x, e->wo.rows, 1, D};
+    o.njobs = 1;
+    o.n = QD;
+    o.total_rows = e->wo.rows;
+    CHECK(launch_matvec(o, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+    CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
+                               nullptr, 0, nullptr, nullptr, 0, st));
+    MatJobs up{};
+    up.job[0] = {e->w1.layer_w(l), e->w1.layer_s(l), nullptr, e->hb, e->w1.rows, 0, HID};
+    up.job[1] = {e->w3.layer_w(l), e->w3.layer_s(l), nullptr, e->hb2, e->w3.rows, 0, HID};
+    up.njobs = 2;
+    up.n = D;
+    up.total_rows = e->w1.rows + e->w3.rows;
+    CHECK(launch_matvec(up, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+    CHECK(launch_swiglu_quantize(e->hb, e->hb2, HID, HID, e->bias, n, e->xq, XQ, e->xs, XS, st));
+    MatJobs down{};
+    down.job[0] = {e->w2.layer_w(l), e->w2.layer_s(l), nullptr, e->x, e->w2.rows, 1, D};
+    down.njobs = 1;
+    down.n = HID;
+    down.total_rows = e->w2.rows;
+    CHECK(launch_matvec(down, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+  }
+  if (want <= 0) return 0;
+  // forward.js:521-530: the final norm of the wanted tokens, the outlier channels apart, the classifier, the columns
+  CHECK(launch_gather_rows(e->xl, D, e->x, D, e->want_d(), want, D, st));
+  CHECK(launch_norm_quantize(e->xl, D, e->finalW, D, e->eps, e->bias, want, e->xq, XQ, e->xs, XS, e->channels, e->nch,
+                             e->picked, nullptr, 0, st));
+  MatJobs cls{};
+  cls.job[0] = {e->wcls.layer_w(0), e->wcls.layer_s(0), nullptr, e->logits, e->wcls.rows, 0, (int64_t)e->vocab};
+  cls.njobs = 1;
+  cls.n = D;
+  cls.total_rows = e->wcls.rows;
+  CHECK(launch_matvec(cls, e->xq, e->xs, XQ, XS, want, e->relaxed, st));
+  CHECK(launch_add_columns(e->logits, e->vocab, e->columns, e->picked, e->nch, e->nch, e->vocab, want, st));
+  CHECK(launch_argmax(e->argmax, e->logits, e->vocab, e->vocab, want, 1, st));
+  return 0;
+}
+
+int run(b200fwd_engine *e, int n, const int32_t *slots, const int32_t *tokens, const int32_t *pos,
+        const uint8_t *want, float *logits_out, int32_t *argmax_out) {
+  if (n < 1 || n > e->T) return fail(B200FWD_EINVAL, "run: " + std::to_string(n) + " tokens, at most " + std::to_string(e->T));
+  int maxpos = 0, W = 0;
+  for (int i = 0; i < n; i++) {
+    const int s = slots ? slots[i] : 0;
+    if (s < 0 || s >= e->slots) return fail(B200FWD_EINVAL, "run: slot " + std::to_string(s) + " out of range");
+    if (tokens[i] < 0 || tokens[i] >= e->vocab)
+      return fail(B200FWD_EINVAL, "run: token " + std::to_string(tokens[i]) + " outside the vocabulary");
+    if (pos[i] < 0 || pos[i] >= e->seqLen)
+      return fail(B200FWD_EINVAL, "run: position " + std::to_string(pos[i]) + " outside the context of " +
+                                      std::to_string(e->seqLen));
+    for (int j = 0; j < i; j++) {
+      const int sj = slots ? slots[j] : 0;
+      if (sj == s && pos[j] >= pos[i])
+        return fail(B200FWD_EINVAL, "run: the tokens of a slot must come in order of their positions");
+    }
+    maxpos = std::max(maxpos, pos[i]);
+    if (want && want[i]) W++;
+  }
+  if (maxpos >= e->capacity) CHECK(grow(e, maxpos));
+  if (W) CHECK(ensure_logit_rows(e, W));
+  const int T = e->T;
+  int32_t *m = e->meta_h;
+  B200_CUDA(cudaStreamSynchronize(e->stream));  // meta_h is free again
+  for (int i = 0; i < n; i++) {
+    m[i] = tokens[i];
+    m[T + i] = slots ? slots[i] : 0;
+    m[2 * T + i] = pos[i];
+  }
+  for (int i = 0, w = 0; i < n; i++)
+    if (want && want[i]) m[3 * T + w++] = i;
+  B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T) * 4, cudaMemcpyHostToDevice, e->stream));
+  CHECK(forward_device(e, n, W, maxpos + 1));
+  if (W) {
+    if (logits_out)
+      B200_CUDA(cudaMemcpyAsync(logits_out, e->logits, (size_t)W * e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+    if (argmax_out) B200_CUDA(cudaMemcpyAsync(argmax_out, e->argmax, (size_t)W * 4, cudaMemcpyDeviceToHost, e->stream));
+  }
+  B200_CUDA(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
+int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, const b200fwd_options *options,
+                b200fwd_engine *e) {
+  const b200fwd_plan &p = *plan;
+  b200fwd_options opt{};
+  opt.half_keys = -1;
+  opt.slots = 1;
+  if (options) opt = *options;
+  if (opt.slots < 1) opt.slots = 1;
+  e->plan = p;
+  e->plan.freq_cis_real = e->plan.freq_cis_imag = nullptr;
+  e->dim = p.dim; e->hidden = p.hidden_dim; e->layers = p.n_layers; e->heads = p.n_heads; e->kvHeads = p.n_kv_heads;
+  e->hs = p.head_size; e->vocab = p.vocab_size; e->seqLen = p.seq_len;
+  if (e->dim <= 0 || e->hidden <= 0 || e->layers <= 0 || e->heads <= 0 || e->kvHeads <= 0 || e->hs <= 0 ||
+      e->vocab <= 0 || e->seqLen <= 0)
+    return fail(B200FWD_EINVAL, "the plan's sizes must be positive");
+  if (e->heads % e->kvHeads) return fail(B200FWD_EINVAL, "n_heads must be a multiple of n_kv_heads");
+  if (e->hs % 2) return fail(B200FWD_EINVAL, "head_size must be even");
+  e->kvDim = e->kvHeads * e->hs;
+  e->qDim = e->heads * e->hs;
+  if (!p.int8) return fail(B200FWD_EUNSUPPORTED, "the plan does not run on the int8 kernels (plan.int8 is false)");
+  if (e->dim % 32 || e->qDim % 32 || e->kvDim % 32 || e->hidden % 32)
+    return fail(B200FWD_EUNSUPPORTED, "the int8 kernels take rows of whole groups of 32");
+  if (p.n_outliers < 0 || p.n_outliers > B200FWD_MAX_OUTLIERS) return fail(B200FWD_EINVAL, "bad outlier count");
+  if (!p.freq_cis_real || !p.freq_cis_imag) return fail(B200FWD_EINVAL, "the plan has no RoPE tables");
+  e->XQ = std::max(std::max(e->dim, e->hidden), e->qDim);
+  e->relaxed = p.relaxed != 0;
+  e->bias = e->relaxed ? 64 : 0;
+  e->eps = p.rms_norm_eps;
+  // forward.js:203: float16 keys and values where the plan allows it and halfKeys (default: every head has keys of
+  // its own) says so. (forward.js also asks for a shared memory, which every multi-threaded page has.)
+  const bool halfKeys = opt.half_keys < 0 ? (e->kvHeads >= e->heads) : opt.half_keys != 0;
+  e->half = p.half_kv && halfKeys;
+  e->slots = opt.slots;
+  e->T = opt.max_tokens > 0 ? opt.max_tokens : std::max(512, 16 * e->slots);
+  if (e->T > 65535) return fail(B200FWD_EINVAL, "max_tokens above 65535");
+  e->device = opt.device;
+  B200_CUDA(cudaSetDevice(e->device));
+  B200_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  CHECK(prepare_attention());
+  const uint8_t *ck = (const uint8_t *)checkpoint;
+  const bool dev = opt.checkpoint_on_device != 0;
+  CHECK(upload_matrix(e, ck, size, dev, p.token_embedding_table, "token_embedding_table", e->emb));
+  CHECK(upload_matrix(e, ck, size, dev, p.wq, "wq", e->wq));
+  CHECK(upload_matrix(e, ck, size, dev, p.wk, "wk", e->wk));
+  CHECK(upload_matrix(e, ck, size, dev, p.wv, "wv", e->wv));
+  CHECK(upload_matrix(e, ck, size, dev, p.wo, "wo", e->wo));
+  CHECK(upload_matrix(e, ck, size, dev, p.w1, "w1", e->w1));
+  CHECK(upload_matrix(e, ck, size, dev, p.w2, "w2", e->w2));
+  CHECK(upload_matrix(e, ck, size, dev, p.w3, "w3", e->w3));
+  if (p.shared_classifier)
+    e->wcls = e->emb;
+  else
+    CHECK(upload_matrix(e, ck, size, dev, p.wcls, "wcls", e->wcls));
+  const Matrix *shapes[] = {&e->wq, &e->wk, &e->wv, &e->wo, &e->w1, &e->w2, &e->w3};
+  const int want_rows[] = {e->qDim, e->kvDim, e->kvDim, e->dim, e->hidden, e->dim, e->hidden};
+  const int want_n[] = {e->dim, e->dim, e->dim, e->qDim, e->dim, e->hidden, e->dim};
+  for (int i = 0; i < 7; i++)
+    if (shapes[i]->rows != want_rows[i] || shapes[i]->n != want_n[i] || shapes[i]->layers != e->layers)
+      return fail(B200FWD_EINVAL, "a layer matrix's shape does not match the plan's sizes");
+  if (e->emb.rows != e->vocab || e->emb.n != e->dim || e->wcls.rows != e->vocab || e->wcls.n != e->dim)
+    return fail(B200FWD_EINVAL, "the embedding or classifier does not match the plan's sizes");
+  CHECK(upload_floats(e, ck, size, dev, p.rms_att_weight, "rms_att_weight", (int64_t)e->layers * e->dim, &e->attW));
+  CHECK(upload_floats(e, ck, size, dev, p.rms_ffn_weight, "rms_ffn_weight", (int64_t)e->layers * e->dim, &e->ffnW));
+  CHECK(upload_floats(e, ck, size, dev, p.rms_final_weight, "rms_final_weight", e->dim, &e->finalW));
+  const size_t table = (size_t)e->seqLen * (e->hs / 2) * 4;
+  CHECK(alloc(e, (void **)&e->cosT, table));
+  CHECK(alloc(e, (void **)&e->sinT, table));
+  B200_CUDA(cudaMemcpyAsync(e->cosT, p.freq_cis_real, table, cudaMemcpyHostToDevice, e->stream));
+  B200_CUDA(cudaMemcpyAsync(e->sinT, p.freq_cis_imag, table, cudaMemcpyHostToDevice, e->stream));
+  e->nch = p.n_outliers;
+  for (int i = 0; i < e->nch; i++)
+    if (p.outliers[i] < 0 || p.outliers[i] >= e->dim) return fail(B200FWD_EINVAL, "an outlier channel past dim");
+  CHECK(alloc(e, (void **)&e->channels, sizeof(int32_t) * std::max(1, e->nch)));
+  CHECK(alloc(e, (void **)&e->columns, (size_t)std::max(1, e->nch) * e->vocab * 4));
+  if (e->nch) {
+    B200_CUDA(cudaMemcpyAsync(e->channels, p.outliers, sizeof(int32_t) * e->nch, cudaMemcpyHostToDevice, e->stream));
+    CHECK(launch_outlier_columns(e->columns, e->wcls.w, e->wcls.s, 32, e->dim, e->vocab, e->channels, e->nch,
+                                 e->stream));
+  }
+  CHECK(alloc_activations(e));
+  // forward.js:272-273: the cache from kv_start positions (or the caller's first capacity)
+  const int first = opt.capacity > 0 ? opt.capacity : p.kv_start;
+  e->capacity = 0;
+  CHECK(grow(e, std::max(1, std::min(first, e->seqLen)) - 1));
+  B200_CUDA(cudaStreamSynchronize(e->stream));
+  e->backend = std::string("B200 CUDA kernels (sm_100a), int8, ") +
+               (e->relaxed ? "7-bit activations (relaxed)" : "8-bit activations") + ", " +
+               (e->half ? "float16" : "float32") + " keys and values, exact float order" +
+               (e->slots > 1 ? ", " + std::to_string(e->slots) + " slots" : "");
+  e->launches_at_create = launches.load();
+  return 0;
+}
+
+void destroy(b200fwd_engine *e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (void *p : e->allocations) cudaFree(p);
+  if (e->meta_h) cudaFreeHost(e->meta_h);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+template <typename F>
+int guarded(F &&f) {
+  try {
+    return f();
+  } catch (const std::exception &ex) {
+    return fail(B200FWD_EINVAL, std::string("exception: ") + ex.what());
+  } catch (...) {
+    return fail(B200FWD_EINVAL, "unknown exception");
+  }
+}
+
+int set_device(b200fwd_engine *e) {
+  if (!e) return fail(B200FWD_EINVAL, "no engine");
+  B200_CUDA(cudaSetDevice(e->device));
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200fwd_abi_version(void) { return B200FWD_ABI_VERSION; }
+
+int b200fwd_last_error(char *buffer, size_t size) {
+  if (!buffer || size == 0) return B200FWD_EINVAL;
+  const std::string &m = last_error();
+  const size_t n = std::min(size - 1, m.size());
+  std::memcpy(buffer, m.data(), n);
+  buffer[n] = 0;
+  return 0;
+}
+
+int b200fwd_create(const void *checkpoint, size_t size, const b200fwd_plan *plan, const b200fwd_options *options,
+                   b200fwd_engine **out) {
+  return guarded([&] {
+    if (!checkpoint || !plan || !out) return fail(B200FWD_EINVAL, "create: null argument");
+    *out = nullptr;
+    auto *e = new b200fwd_engine();
+    const int rc = make_engine(checkpoint, size, plan, options, e);
+    if (rc) {
+      const std::string keep = last_error();
+      destroy(e);
+      last_error() = keep;
+      return rc;
+    }
+    *out = e;
+    return 0;
+  });
+}
+
+int b200fwd_destroy(b200fwd_engine *engine) {
+  destroy(engine);
+  return 0;
+}
+
+int b200fwd_bind_logits(b200fwd_engine *e, float *logits) {
+  if (!e) return fail(B200FWD_EINVAL, "no engine");
+  e->bound = logits;
+  return 0;
+}
+
+int b200fwd_forward(b200fwd_engine *e, int32_t token, int32_t pos, int32_t need_logits) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    const int32_t slot = 0;
+    const uint8_t want = need_logits ? 1 : 0;
+    e->last_logits.resize(e->vocab);
+    CHECK(run(e, 1, &slot, &token, &pos, &want, need_logits ? e->last_logits.data() : nullptr, nullptr));
+    if (need_logits && e->bound) std::memcpy(e->bound, e->last_logits.data(), sizeof(float) * e->vocab);
+    return 0;
+  });
+}
+
+int b200fwd_forward_many(b200fwd_engine *e, const int32_t *tokens, int32_t count, int32_t pos) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (count < 0 || (count > 0 && !tokens)) return fail(B200FWD_EINVAL, "forward_many: bad tokens");
+    std::vector<int32_t> slots(e->T, 0), p(e->T);
+    for (int at = 0; at < count; at += e->T) {
+      const int n = std::min(e->T, count - at);
+      for (int i = 0; i < n; i++) p[i] = pos + at + i;
+      CHECK(run(e, n, slots.data(), tokens + at, p.data(), nullptr, nullptr, nullptr));
+    }
+    return 0;
+  });
+}
+
+int b200fwd_prompt_block(b200fwd_engine *e, int32_t *out) {
+  if (!e || !out) return fail(B200FWD_EINVAL, "prompt_block: null argument");
+  *out = e->T;
+  return 0;
+}
+
+int b200fwd_keys_values(b200fwd_engine *e, int32_t slot, int32_t from, int32_t count, float *keys, float *values) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (slot < 0 || slot >= e->slots || from < 0 || count < 0 || from + count > e->capacity || !keys || !values)
+      return fail(B200FWD_EINVAL, "keys_values: out of range");
+    const size_t row = (size_t)e->kvDim * e->esize();
+    std::vector<uint8_t> raw((size_t)count * row);
+    for (int l = 0; l < e->layers; l++) {
+      for (int kv = 0; kv < 2; kv++) {
+        const uint8_t *src = e->cache + ((((int64_t)slot * e->layers + l) * 2 + kv) * e->capacity + from) * row;
+        B200_CUDA(cudaMemcpy(raw.data(), src, raw.size(), cudaMemcpyDeviceToHost));
+        float *dst = (kv ? values : keys) + (size_t)l * count * e->kvDim;
+        const size_t total = (size_t)count * e->kvDim;
+        if (e->half) {
+          const uint16_t *h = reinterpret_cast<const uint16_t *>(raw.data());
+          for (size_t i = 0; i < total; i++) dst[i] = half_bits_to_float(h[i]);
+        } else {
+          std::memcpy(dst, raw.data(), total * 4);
+        }
+      }
+    }
+    return 0;
+  });
+}
+
+int b200fwd_logits(b200fwd_engine *e, float *out) {
+  if (!e || !out) return fail(B200FWD_EINVAL, "logits: null argument");
+  if (e->last_logits.empty()) std::memset(out, 0, sizeof(float) * e->vocab);
+  else std::memcpy(out, e->last_logits.data(), sizeof(float) * e->vocab);
+  return 0;
+}
+
+int b200fwd_backend(b200fwd_engine *e, char *buffer, size_t size) {
+  if (!e || !buffer || !size) return fail(B200FWD_EINVAL, "backend: null argument");
+  const size_t n = std::min(size - 1, e->backend.size());
+  std::memcpy(buffer, e->backend.data(), n);
+  buffer[n] = 0;
+  return 0;
+}
+
+int b200fwd_memory_bytes(b200fwd_engine *e, uint64_t *out) {
+  if (!e || !out) return fail(B200FWD_EINVAL, "memory_bytes: null argument");
+  *out = e->bytes;
+  return 0;
+}
+
+int b200fwd_run(b200fwd_engine *e, int32_t n, const int32_t *slots, const int32_t *tokens, const int32_t *pos,
+                const uint8_t *want, float *logits, int32_t *argmax) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (!tokens || !pos) return fail(B200FWD_EINVAL, "run: null tokens or positions");
+    return run(e, n, slots, tokens, pos, want, logits, argmax);
+  });
+}
+
+int b200fwd_reset_slot(b200fwd_engine *e, int32_t slot) {
+  if (!e || slot < 0 || slot >= e->slots) return fail(B200FWD_EINVAL, "reset_slot: out of range");
+  return 0;  // positions are the caller's: the next run at position 0 writes over the cache
+}
+
+int b200fwd_stream_of(b200fwd_engine *e, b200fwd_stream *out) {
+  if (!e || !out) return fail(B200FWD_EINVAL, "stream_of: null argument");
+  *out = reinterpret_cast<b200fwd_stream>(e->stream);
+  return 0;
+}
+
+int b200fwd_launch_count(b200fwd_engine *e, uint64_t *out) {
+  if (!e || !out) return fail(B200FWD_EINVAL, "launch_count: null argument");
+  *out = launches.load() - e->launches_at_create;
+  return 0;
+}
+
+int b200fwd_generate_greedy(b200fwd_engine *e, int32_t n, const int32_t *slots, const int32_t *first,
+                            const int32_t *pos0, int32_t steps, int32_t *out) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (n < 1 || n > std::min(e->T, 1024) || steps < 1 || !slots || !first || !pos0 || !out)
+      return fail(B200FWD_EINVAL, "generate_greedy: bad arguments");
+    int maxpos = 0;
+    for (int i = 0; i < n; i++) {
+      if (slots[i] < 0 || slots[i] >= e->slots) return fail(B200FWD_EINVAL, "generate_greedy: slot out of range");
+      for (int j = 0; j < i; j++)
+        if (slots[j] == slots[i]) return fail(B200FWD_EINVAL, "generate_greedy: a slot given twice");
+      if (first[i] < 0 || first[i] >= e->vocab) return fail(B200FWD_EINVAL, "generate_greedy: token out of range");
+      if (pos0[i] < 0 || pos0[i] + steps > e->seqLen)
+        return fail(B200FWD_EINVAL, "generate_greedy: the steps run past the context");
+      maxpos = std::max(maxpos, pos0[i] + steps - 1);
+    }
+    if (maxpos >= e->capacity) CHECK(grow(e, maxpos));
+    CHECK(ensure_logit_rows(e, n));
+    if (e->history_len < n * steps) {
+      B200_CUDA(cudaStreamSynchronize(e->stream));
+      release(e, e->history, (size_t)e->history_len * 4);
+      e->history = nullptr;
+      CHECK(alloc(e, (void **)&e->history, (size_t)n * steps * 4));
+      e->history_len = n * steps;
+    }
+    const int T = e->T;
+    int32_t *m = e->meta_h;
+    B200_CUDA(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n; i++) {
+      m[i] = first[i];
+      m[T + i] = slots[i];
+      m[2 * T + i] = pos0[i];
+      m[3 * T + i] = i;
+    }
+    m[4 * T] = 0;
+    m[4 * T + 1] = 0;
+    B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T + 2) * 4, cudaMemcpyHostToDevice, e->stream));
+    // one step, captured once and replayed: the forward pass of every slot's token, the argmax, and the step's
+    // bookkeeping (the argmax becomes the next token, the positions move on), with no host in between
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const uint64_t before = launches.load();
+    B200_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = forward_device(e, n, n, e->capacity);
+    if (!rc)
+      rc = launch_advance(e->tokens_d(), e->pos_d(), e->argmax, e->history, steps, e->step_d(), n, e->logits, e->vocab,
+                          e->bad_d(), e->stream);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+    const uint64_t per_step = launches.load() - before;
+    launches.fetch_sub(per_step);  // counted below as they replay
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    for (int s = 0; s < steps; s++) {
+      ce = cudaGraphLaunch(exec, e->stream);
+      if (ce != cudaSuccess) break;
+      launches.fetch_add(per_step);
+    }
+    cudaError_t se = cudaStreamSynchronize(e->stream);
+    cudaGraphExecDestroy(exec);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphLaunch");
+    if (se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
+    B200_CUDA(cudaMemcpy(out, e->history, (size_t)n * steps * 4, cudaMemcpyDeviceToHost));
+    int32_t bad = 0;
+    B200_CUDA(cudaMemcpy(&bad, e->bad_d(), 4, cudaMemcpyDeviceToHost));
+    if (bad)
+      return fail(B200FWD_ENOTFINITE,
+                  "The model computed logits that are not finite numbers (NaN or infinity), so no token can be drawn.");
+    return 0;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,810 @@
+// kernels.cu — the hot-path kernels of the forward pass for sm_100a, each the number of its reference kernel to the
+// bit (kernels/kernel.ts, kernels/kernel_relaxed.ts), and their launchers.
+//
+// Built with --fmad=false; every float step is written with the rounding intrinsics of exact.cuh.
+#include <algorithm>
+#include <cfloat>
+#include <cstdint>
+
+#include "common.h"
+#include "exact.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int MV_WARPS = 8;
+constexpr size_t MAX_SOFTMAX_SMEM = 200 * 1024;
+
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+// the exact integer of one group's 32 products
+__device__ __forceinline__ int dot_group(const uint4 &wa, const uint4 &wb, const uint4 &xa, const uint4 &xb, int c) {
+  c = dp4a(wa.x, xa.x, c);
+  c = dp4a(wa.y, xa.y, c);
+  c = dp4a(wa.z, xa.z, c);
+  c = dp4a(wa.w, xa.w, c);
+  c = dp4a(wb.x, xb.x, c);
+  c = dp4a(wb.y, xb.y, c);
+  c = dp4a(wb.z, xb.z, c);
+  return dp4a(wb.w, xb.w, c);
+}
+
+// kernel.ts:222-226 dot32's lanes: lane k holds products 2k, 2k+1, 2k+8, 2k+9 of each half of 16
+__device__ __forceinline__ void dot32_lanes(const uint4 &wa, const uint4 &wb, const uint4 &xa, const uint4 &xb,
+                                            int L[4]) {
+  const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  const uint32_t x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int lo = k >> 1;                      // words 0/2 (k = 0, 1) or 1/3 (k = 2, 3) of a half
+    const uint32_t sel = (k & 1) ? 0x7632u : 0x5410u;  // the low or high two bytes of each word
+    int s = 0;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t ww = __byte_perm(w[4 * h + lo], w[4 * h + lo + 2], sel);
+      const uint32_t xx = __byte_perm(x[4 * h + lo], x[4 * h + lo + 2], sel);
+      s = dp4a(ww, xx, s);
+    }
+    L[k] = s;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T pick3(int j, T a, T b, T c) { return j == 0 ? a : (j == 1 ? b : c); }
+
+// The int8 matmul of count tokens (MT at a time), one warp a row. Each lane takes groups lane, lane+32, ...: their
+// exact integers, each times (weight scale x activation scale) rounded once, go to shared memory; then lanes
+// 4t..4t+3 add token t's chains in the reference's order:
+//  relaxed (kernel_relaxed.ts:34-67): lane k the groups 4j+k below the last four, the lanes ((0+1)+2)+3, then the
+//    groups past the fours one at a time;
+//  8-bit (kernel.ts:231-251): lane k dot32's lane k of every group, then ((0+1)+2)+3.
+template <int MT, bool RELAXED>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+    matvec_kernel(MatJobs jobs, const int8_t *__restrict__ xq, const float *__restrict__ xs, int64_t q_stride,
+                  int64_t s_stride, int count) {
+  constexpr int LANES = RELAXED ? 1 : 4;
+  __shared__ float buf[MV_WARPS][MT][LANES][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = jobs.n, ng = n >> 5, ng4 = ng & ~3;
+  const int ct = lane >> 2, ck = lane & 3;
+  for (int row = blockIdx.x * MV_WARPS + warp; row < jobs.total_rows; row += gridDim.x * MV_WARPS) {
+    int j = 0, r = row;
+    if (jobs.njobs > 1 && r >= jobs.job[0].rows) {
+      r -= jobs.job[0].rows;
+      j = 1;
+      if (jobs.njobs > 2 && r >= jobs.job[1].rows) {
+        r -= jobs.job[1].rows;
+        j = 2;
+      }
+    }
+    const int8_t *wrow = pick3(j, jobs.job[0].w, jobs.job[1].w, jobs.job[2].w) + (int64_t)r * n;
+    const float *srow = pick3(j, jobs.job[0].s, jobs.job[1].s, jobs.job[2].s) + (int64_t)r * ng;
+    const int32_t *cbase = pick3(j, jobs.job[0].c, jobs.job[1].c, jobs.job[2].c);
+    const int32_t *crow = cbase ? cbase + (int64_t)r * ng : nullptr;
+    float *out = pick3(j, jobs.job[0].out, jobs.job[1].out, jobs.job[2].out) + r;
+    const int64_t ostride = pick3(j, jobs.job[0].out_stride, jobs.job[1].out_stride, jobs.job[2].out_stride);
+    const int accumulate = pick3(j, jobs.job[0].accumulate, jobs.job[1].accumulate, jobs.job[2].accumulate);
+    for (int t0 = 0; t0 < count; t0 += MT) {
+      const int mt = min(MT, count - t0);
+      float acc = 0.0f;
+      for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        if (g < ng) {
+          const uint4 wa = __ldg(reinterpret_cast<const uint4 *>(wrow + (int64_t)g * 32));
+          const uint4 wb = __ldg(reinterpret_cast<const uint4 *>(wrow + (int64_t)g * 32 + 16));
+          const float sw = __ldg(srow + g);
+          int corr = 0;
+          if (RELAXED) {
+            if (crow) {
+              corr = __ldg(crow + g);
+            } else {
+              // -64 times the group's sum (int8_sums, kernel.ts:204-212): dot(w, q) + corr = dot(w, q - 64)
+              const uint4 ones = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+              corr = -64 * dot_group(wa, wb, ones, ones, 0);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < MT; t++) {
+            if (t < mt) {
+              const int8_t *xrow = xq + (int64_t)(t0 + t) * q_stride + (int64_t)g * 32;
+              const uint4 xa = *reinterpret_cast<const uint4 *>(xrow);
+              const uint4 xb = *reinterpret_cast<const uint4 *>(xrow + 16);
+              const float sc = fmul(sw, xs[(int64_t)(t0 + t) * s_stride + g]);
+              if (RELAXED) {
+                const int S = dot_group(wa, wb, xa, xb, corr);
+                buf[warp][t][0][lane] = fmul(__int2float_rn(S), sc);
+              } else {
+                int L[4];
+                dot32_lanes(wa, wb, xa, xb, L);
+#pragma unroll
+                for (int k = 0; k < 4; k++) buf[warp][t][k % LANES][lane] = fmul(__int2float_rn(L[k]), sc);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (ct < mt) {
+          if (RELAXED) {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              if (g0 + ck + 4 * i < ng4) acc = fadd(acc, buf[warp][ct][0][ck + 4 * i]);
+          } else {
+            for (int i = 0; i < 32 && g0 + i < ng; i++) acc = fadd(acc, buf[warp][ct][ck % LANES][i]);
+          }
+        }
+        __syncwarp();
+      }
+      const float a1 = __shfl_down_sync(FULL, acc, 1);
+      const float a2 = __shfl_down_sync(FULL, acc, 2);
+      const float a3 = __shfl_down_sync(FULL, acc, 3);
+      if (ck == 0 && ct < mt) {
+        float sum = fadd(fadd(fadd(acc, a1), a2), a3);
+        if (RELAXED) {
+          const int last = ((ng - 1) >> 5) << 5;  // the last round's first group; the tail groups are in it
+          for (int g = ng4; g < ng; g++) sum = fadd(sum, buf[warp][ct][0][g - last]);
+        }
+        float *o = out + (int64_t)(t0 + ct) * ostride;
+        *o = accumulate ? fadd(*o, sum) : sum;
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// one group of 32 values (a lane each) quantized as kernel.ts:129-156: groupMax's lane-class maxima, then the
+// scalar comparisons; the scale, its inverse, and each value's rounding
+__device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8_t *xq, float *xs) {
+  float m = fabsf(v);
+  m = wmax(m, __shfl_xor_sync(FULL, m, 4));
+  m = wmax(m, __shfl_xor_sync(FULL, m, 8));
+  m = wmax(m, __shfl_xor_sync(FULL, m, 16));
+  const float m0 = __shfl_sync(FULL, m, 0), m1 = __shfl_sync(FULL, m, 1);
+  const float m2 = __shfl_sync(FULL, m, 2), m3 = __shfl_sync(FULL, m, 3);
+  float amax = m0;
+  if (m1 > amax) amax = m1;
+  if (m2 > amax) amax = m2;
+  if (m3 > amax) amax = m3;
+  const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
+  const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
+  xq[lane] = quantize_one(v, inv, bias);
+  if (lane == 0) *xs = scale;
+}
+
+// kernel.ts:330-342 rmsnorm's scale: four lane chains over the fours, ((0+1)+2)+3, the rest one by one
+__device__ __forceinline__ float norm_scale(const float *x, int n, float eps, float *part) {
+  const int n4 = n & ~3;
+  if (threadIdx.x < 4) {
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < n4; j += 4) {
+      const float v = x[j];
+      acc = fadd(acc, fmul(v, v));
+    }
+    part[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
+    for (int j = n4; j < n; j++) ss = fadd(ss, fmul(x[j], x[j]));
+    part[4] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)n), eps)));
+  }
+  __syncthreads();
+  return part[4];
+}
+
+__global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias,
+                                     int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride,
+                                     const int32_t *channels, int nch, float *picked, float *out_f,
+                                     int64_t out_stride) {
+  __shared__ float part[5];
+  const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const float *xr = x + (int64_t)tok * x_stride;
+  const float s = norm_scale(xr, n, eps, part);
+  const int ng = n >> 5;
+  for (int g = warp; g < ng; g += warps) {
+    const int j = g * 32 + lane;
+    float v = fmul(w[j], fmul(s, xr[j]));
+    if (out_f) out_f[(int64_t)tok * out_stride + j] = v;
+    for (int c = 0; c < nch; c++) {
+      if (channels[c] == j) {
+        picked[(int64_t)tok * nch + c] = v;
+        v = 0.0f;
+      }
+    }
+    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+  }
+}
+
+__global__ void rmsnorm_kernel(float *out, const float *x, const float *w, int n, float eps, int64_t stride) {
+  __shared__ float part[5];
+  const float *xr = x + (int64_t)blockIdx.x * stride;
+  const float s = norm_scale(xr, n, eps, part);
+  for (int j = threadIdx.x; j < n; j += blockDim.x) out[(int64_t)blockIdx.x * stride + j] = fmul(w[j], fmul(s, xr[j]));
+}
+
+__global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh, int hs, int rot) {
+  const int turned = rot > 0 && rot < hs ? rot : hs;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int h = idx / (turned / 2), i = 2 * (idx % (turned / 2));
+  if (h >= nh) return;
+  float *base = v + h * hs + i;
+  const float v0 = base[0], v1 = base[1], c = fcr[i >> 1], s = fci[i >> 1];
+  base[0] = fsub(fmul(v0, c), fmul(v1, s));
+  base[1] = fadd(fmul(v0, s), fmul(v1, c));
+}
+
+__global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq,
+                                int64_t q_stride, float *xs, int64_t s_stride) {
+  const int lane = threadIdx.x & 31;
+  const int ng = n >> 5;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= (int64_t)ng * count) return;
+  const int tok = (int)(gw / ng), g = (int)(gw % ng);
+  const float v = x[(int64_t)tok * x_stride + g * 32 + lane];
+  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+}
+
+// kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x
+__global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int count,
+                                       int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride) {
+  const int lane = threadIdx.x & 31;
+  const int ng = n >> 5, n4 = n & ~3;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= (int64_t)ng * count) return;
+  const int tok = (int)(gw / ng), g = (int)(gw % ng);
+  const int j = g * 32 + lane;
+  const float v = h1[(int64_t)tok * stride + j];
+  const float e = j < n4 ? vexp(-v) : fexp(-v);
+  const float o = fmul(fdiv(v, fadd(1.0f, e)), h3[(int64_t)tok * stride + j]);
+  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+}
+
+__global__ void embed_kernel(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim,
+                             float *x, int64_t x_stride) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)count * dim) return;
+  const int t = (int)(i / dim), j = (int)(i % dim);
+  const int64_t at = (int64_t)tokens[t] * dim + j;
+  x[(int64_t)t * x_stride + j] = fmul((float)w[at], s[at / group]);
+}
+
+__global__ void rope_cache_kernel(float *q, int64_t q_stride, const float *k, const float *v, int64_t kv_stride,
+                                  const float *cos, const float *sin, const int32_t *pos, const int32_t *seq,
+                                  uint8_t *kc, uint8_t *vc, int64_t seq_stride, int half, int nh, int nkv, int hs,
+                                  int rot) {
+  const int tok = blockIdx.y;
+  const int p = pos[tok];
+  const int64_t sq = seq[tok];
+  const int hp = hs / 2, kvDim = nkv * hs;
+  const int turned = rot > 0 && rot < hs ? rot : hs;
+  const float *cr = cos + (int64_t)p * hp, *sr = sin + (int64_t)p * hp;
+  const int esize = half ? 2 : 4;
+  const int64_t cache_at = (sq * seq_stride + (int64_t)p * kvDim) * esize;
+  const int total = (nh + nkv) * hp + kvDim;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    if (idx < (nh + nkv) * hp) {
+      const bool isq = idx < nh * hp;
+      const int local = isq ? idx : idx - nh * hp;
+      const int h = local / hp, i = 2 * (local % hp);
+      float v0, v1;
+      if (isq) {
+        float *base = q + (int64_t)tok * q_stride + h * hs + i;
+        v0 = base[0];
+        v1 = base[1];
+        if (i < turned) {
+          const float c = cr[i >> 1], s = sr[i >> 1];
+          base[0] = fsub(fmul(v0, c), fmul(v1, s));
+          base[1] = fadd(fmul(v0, s), fmul(v1, c));
+        }
+      } else {
+        const float *base = k + (int64_t)tok * kv_stride + h * hs + i;
+        v0 = base[0];
+        v1 = base[1];
+        float o0 = v0, o1 = v1;
+        if (i < turned) {
+          const float c = cr[i >> 1], s = sr[i >> 1];
+          o0 = fsub(fmul(v0, c), fmul(v1, s));
+          o1 = fadd(fmul(v0, s), fmul(v1, c));
+        }
+        const int64_t e = cache_at + (int64_t)(h * hs + i) * esize;
+        if (half) {
+          reinterpret_cast<uint16_t *>(kc + e)[0] = float_to_half(o0);
+          reinterpret_cast<uint16_t *>(kc + e)[1] = float_to_half(o1);
+        } else {
+          reinterpret_cast<float *>(kc + e)[0] = o0;
+          reinterpret_cast<float *>(kc + e)[1] = o1;
+        }
+      }
+    } else {
+      const int j = idx - (nh + nkv) * hp;
+      const float val = v[(int64_t)tok * kv_stride + j];
+      const int64_t e = cache_at + (int64_t)j * esize;
+      if (half)
+        *reinterpret_cast<uint16_t *>(vc + e) = float_to_half(val);
+      else
+        *reinterpret_cast<float *>(vc + e) = val;
+    }
+  }
+}
+
+template <bool HALF>
+__device__ __forceinline__ float kv_at(const void *base, int64_t i) {
+  if (HALF) return half_to_float(reinterpret_cast<const uint16_t *>(base)[i]);
+  return reinterpret_cast<const float *>(base)[i];
+}
+
+// kernel.ts:462-498 the scores of one block of ATTN_CHUNK positions, every query head of one kv head: a thread a
+// position, four lane accumulators per head over the fours of the head, summed (l0+l2)+(l1+l3), the rest after;
+// times 1/sqrt(hs).
+template <bool HALF>
+__global__ void attn_scores_kernel(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
+                                   const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs,
+                                   int h0, int h1) {
+  extern __shared__ float smem[];
+  const int tok = blockIdx.z, kvh = blockIdx.y, chunk = blockIdx.x;
+  const int count = (pos ? pos[tok] : pos0) + 1;
+  const int t0 = chunk * ATTN_CHUNK;
+  if (t0 >= count) return;
+  const int G = nh / nkv, kvDim = nkv * hs, hs4 = hs & ~3;
+  const int64_t sbase = (int64_t)(seq ? seq[tok] : 0) * seq_stride;
+  float *qs = smem;  // [G][hs]
+  for (int i = threadIdx.x; i < G * hs; i += blockDim.x) qs[i] = q[(int64_t)tok * q_stride + kvh * G * hs + i];
+  __syncthreads();
+  const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
+  const int t = t0 + threadIdx.x;
+  const bool valid = t < count;
+  const int64_t krow = sbase + (int64_t)t * kvDim + (int64_t)kvh * hs;
+  for (int g = 0; g < G; g++) {
+    const int h = kvh * G + g;
+    const bool want = valid && h >= h0 && h < h1;
+    if (want) {
+      const float *qh = qs + g * hs;
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+      int j = 0;
+      for (; j < hs4; j += 4) {
+        a0 = fadd(a0, fmul(qh[j], kv_at<HALF>(kc, krow + j)));
+        a1 = fadd(a1, fmul(qh[j + 1], kv_at<HALF>(kc, krow + j + 1)));
+        a2 = fadd(a2, fmul(qh[j + 2], kv_at<HALF>(kc, krow + j + 2)));
+        a3 = fadd(a3, fmul(qh[j + 3], kv_at<HALF>(kc, krow + j + 3)));
+      }
+      float s = fadd(fadd(a0, a2), fadd(a1, a3));
+      for (; j < hs; j++) s = fadd(s, fmul(qh[j], kv_at<HALF>(kc, krow + j)));
+      att[((int64_t)tok * nh + h) * P + t] = fmul(s, isq);
+    }
+  }
+}
+
+// kernel.ts:499-521 softmax of one head: the largest, exp of every score less it (vexp on the fours, fexp after),
+// the sum in four lane chains ((0+1)+2)+3 then the rest one by one, and every weight times 1/sum
+__global__ void attn_softmax_kernel(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1) {
+  extern __shared__ float e[];
+  __shared__ float part[5];
+  __shared__ float wm[32];
+  const int tok = blockIdx.y, h = blockIdx.x;
+  if (h < h0 || h >= h1) return;
+  const int count = (pos ? pos[tok] : pos0) + 1, count4 = count & ~3;
+  float *row = att + ((int64_t)tok * nh + h) * P;
+  // the largest from -FLT_MAX, a NaN kept (kernel.ts:423-445: the order does not matter)
+  float mx = -FLT_MAX;
+  for (int t = threadIdx.x; t < count; t += blockDim.x) mx = wmax(mx, row[t]);
+  for (int o = 16; o > 0; o >>= 1) mx = wmax(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -FLT_MAX;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = wmax(mx, wm[w]);
+  for (int t = threadIdx.x; t < count; t += blockDim.x) {
+    const float d = fsub(row[t], mx);
+    e[t] = t < count4 ? vexp(d) : fexp(d);
+  }
+  __syncthreads();
+  if (threadIdx.x < 4) {
+    float acc = 0.0f;
+    for (int t = threadIdx.x; t < count4; t += 4) acc = fadd(acc, e[t]);
+    part[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
+    for (int t = count4; t < count; t++) sum = fadd(sum, e[t]);
+    part[4] = fdiv(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = part[4];
+  for (int t = threadIdx.x; t < count; t += blockDim.x) row[t] = fmul(e[t], inv);
+}
+
+// kernel.ts:522-565 the weighted sum of the values: per output, positions in fours ((w0 v0 + w1 v1) + (w2 v2 +
+// w3 v3)) added in order (a value past the fours of the head: the adds one after another), then the positions
+// past the fours one at a time. A thread takes two neighbouring values of one head.
+template <bool HALF>
+__global__ void attn_values_kernel(float *out, int64_t out_stride, const void *vc, const float *att,
+                                   const int32_t *seq, const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh,
+                                   int nkv, int hs, int h0, int h1) {
+  const int tok = blockIdx.y, kvh = blockIdx.x;
+  const int G = nh / nkv, hp = (hs + 1) / 2, kvDim = nkv * hs, hs4 = hs & ~3;
+  const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
+  if (g >= G) return;
+  const int h = kvh * G + g;
+  if (h < h0 || h >= h1) return;
+  const int count = (pos ? pos[tok] : pos0) + 1, count4 = count & ~3;
+  const int64_t sbase = (int64_t)(seq ? seq[tok] : 0) * seq_stride + (int64_t)kvh * hs;
+  const float *w = att + ((int64_t)tok * nh + h) * P;
+  const int j0 = 2 * jp, j1 = j0 + 1;
+  const bool has1 = j1 < hs;
+  float o0 = 0.0f, o1 = 0.0f;
+  int t = 0;
+  for (; t < count4; t += 4) {
+    const float4 wt = make_float4(w[t], w[t + 1], w[t + 2], w[t + 3]);
+    const int64_t r0 = sbase + (int64_t)t * kvDim;
+    const float v00 = kv_at<HALF>(vc, r0 + j0), v10 = kv_at<HALF>(vc, r0 + kvDim + j0);
+    const float v20 = kv_at<HALF>(vc, r0 + 2 * kvDim + j0), v30 = kv_at<HALF>(vc, r0 + 3 * kvDim + j0);
+    if (j0 < hs4) {
+      o0 = fadd(o0, fadd(fadd(fmul(wt.x, v00), fmul(wt.y, v10)), fadd(fmul(wt.z, v20), fmul(wt.w, v30))));
+    } else {
+      o0 = fadd(fadd(fadd(fadd(o0, fmul(wt.x, v00)), fmul(wt.y, v10)), fmul(wt.z, v20)), fmul(wt.w, v30));
+    }
+    if (has1) {
+      const float v01 = kv_at<HALF>(vc, r0 + j1), v11 = kv_at<HALF>(vc, r0 + kvDim + j1);
+      const float v21 = kv_at<HALF>(vc, r0 + 2 * kvDim + j1), v31 = kv_at<HALF>(vc, r0 + 3 * kvDim + j1);
+      if (j1 < hs4) {
+        o1 = fadd(o1, fadd(fadd(fmul(wt.x, v01), fmul(wt.y, v11)), fadd(fmul(wt.z, v21), fmul(wt.w, v31))));
+      } else {
+        o1 = fadd(fadd(fadd(fadd(o1, fmul(wt.x, v01)), fmul(wt.y, v11)), fmul(wt.z, v21)), fmul(wt.w, v31));
+      }
+    }
+  }
+  for (; t < count; t++) {
+    const float wt = w[t];
+    const int64_t r0 = sbase + (int64_t)t * kvDim;
+    o0 = fadd(o0, fmul(wt, kv_at<HALF>(vc, r0 + j0)));
+    if (has1) o1 = fadd(o1, fmul(wt, kv_at<HALF>(vc, r0 + j1)));
+  }
+  float *o = out + (int64_t)tok * out_stride + h * hs;
+  o[j0] = o0;
+  if (has1) o[j1] = o1;
+}
+
+__global__ void add_columns_kernel(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride,
+                                   int nc, int n, int count) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * count) return;
+  const int tok = (int)(i / n), j = (int)(i % n);
+  float v = y[(int64_t)tok * y_stride + j];
+  for (int c = 0; c < nc; c++) v = fadd(v, fmul(a[(int64_t)tok * a_stride + c], rows[(int64_t)c * n + j]));
+  y[(int64_t)tok * y_stride + j] = v;
+}
+
+// (value, index) better than (value2, index2) for argmax: mode 0 kernel.ts's `>` scan (NaN never taken), mode 1
+// numpy's (the first NaN wins); ties to the lower index
+__device__ __forceinline__ bool better(float a, int ia, float b, int ib, int mode) {
+  const bool na = a != a, nb = b != b;
+  if (mode == 1) {
+    if (na != nb) return na;
+    if (na && nb) return ia < ib;
+  } else {
+    if (na != nb) return nb;
+    if (na && nb) return ia < ib;
+  }
+  if (a != b) return a > b;
+  return ia < ib;
+}
+
+__global__ void argmax_kernel(int32_t *out, const float *x, int64_t stride, int n, int mode) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int tok = blockIdx.x;
+  const float *r = x + (int64_t)tok * stride;
+  float bv = 0.0f;
+  int bi = -1;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float v = r[j];
+    if (bi < 0 || better(v, j, bv, bi, mode)) { bv = v; bi = j; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL, bv, o);
+    const int oi = __shfl_xor_sync(FULL, bi, o);
+    if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi, mode))) { bv = ov; bi = oi; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+      if (si[w] >= 0 && (bi < 0 || better(sv[w], si[w], bv, bi, mode))) { bv = sv[w]; bi = si[w]; }
+    // kernel.ts's scan starts from x[0]: a NaN there is never replaced
+    if (mode == 0 && r[0] != r[0]) bi = 0;
+    out[tok] = bi;
+  }
+}
+
+__global__ void gather_rows_kernel(float *dst, int64_t dst_stride, const float *src, int64_t src_stride,
+                                   const int32_t *idx, int count, int dim) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)count * dim) return;
+  const int t = (int)(i / dim), j = (int)(i % dim);
+  dst[(int64_t)t * dst_stride + j] = src[(int64_t)idx[t] * src_stride + j];
+}
+
+__global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+                                       const int32_t *channels, int nch) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)vocab * nch) return;
+  const int c = (int)(i / vocab), v = (int)(i % vocab);
+  const int ch = channels[c];
+  const int groups = dim / group;
+  cols[i] = fmul((float)w[(int64_t)v * dim + ch], s[(int64_t)v * groups + ch / group]);
+}
+
+__global__ void to_f16_kernel(uint16_t *out, const float *x, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = float_to_half(x[i]);
+}
+__global__ void from_f16_kernel(float *out, const uint16_t *x, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = half_to_float(x[i]);
+}
+__global__ void add_inplace_kernel(float *x, const float *y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = fadd(x[i], y[i]);
+}
+__global__ void swiglu_kernel(float *out, const float *h1, const float *h3, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = h1[i];
+  const float e = i < (n & ~(int64_t)3) ? vexp(-v) : fexp(-v);
+  out[i] = fmul(fdiv(v, fadd(1.0f, e)), h3[i]);
+}
+__global__ void int8_sums_kernel(int32_t *out, const int8_t *w, int64_t groups) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  int s = 0;
+  for (int j = 0; j < 32; j++) s += w[g * 32 + j];
+  out[g] = -64 * s;
+}
+__global__ void advance_kernel(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps,
+                               int32_t *step, int count, const float *logits, int64_t vocab, int32_t *bad) {
+  const int i = threadIdx.x;
+  const int at = *step;
+  __syncthreads();
+  if (i < count) {
+    const int32_t id = ids[i];
+    const float v = logits[(int64_t)i * vocab + id];
+    // llama2_numpy.greedy (public/llama2_numpy.py:1521-1527): a largest logit that is no finite number stops
+    if (!(v == v) || v == INFINITY || v == -INFINITY) atomicExch(bad, 1);
+    tokens[i] = id;
+    pos[i] += 1;
+    if (at < steps) history[(int64_t)i * steps + at] = id;
+  }
+  if (i == 0) *step = at + 1;
+}
+
+#define CHECK_RC(expr)      \
+  do {                      \
+    int rc_ = (expr);       \
+    if (rc_) return rc_;    \
+  } while (0)
+
+inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+}  // namespace
+
+int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_t q_stride, int64_t s_stride,
+                  int count, bool relaxed, cudaStream_t stream) {
+  if (count <= 0 || jobs.total_rows <= 0) return 0;
+  if (jobs.n % 32) return fail(B200FWD_EINVAL, "matvec: n must be whole groups of 32");
+  const unsigned grid = std::min<unsigned>(blocks_for(jobs.total_rows, MV_WARPS), 148u * 32u);
+  const int mt = count >= 8 ? 8 : count >= 4 ? 4 : count >= 2 ? 2 : 1;
+#define B200_MV(MT, R) matvec_kernel<MT, R><<<grid, MV_WARPS * 32, 0, stream>>>(jobs, xq, xs, q_stride, s_stride, count)
+  if (relaxed) {
+    switch (mt) {
+      case 8: B200_MV(8, true); break;
+      case 4: B200_MV(4, true); break;
+      case 2: B200_MV(2, true); break;
+      default: B200_MV(1, true); break;
+    }
+  } else {
+    switch (mt) {
+      case 8: B200_MV(8, false); break;
+      case 4: B200_MV(4, false); break;
+      case 2: B200_MV(2, false); break;
+      default: B200_MV(1, false); break;
+    }
+  }
+#undef B200_MV
+  B200_LAUNCHED("matvec_kernel");
+  return 0;
+}
+
+int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
+                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
+                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
+  norm_quantize_kernel<<<count, 256, 0, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, channels,
+                                                  nch, picked, out_f, out_stride);
+  B200_LAUNCHED("norm_quantize_kernel");
+  return 0;
+}
+
+int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
+                    float *xs, int64_t s_stride, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (n % 32) return fail(B200FWD_EINVAL, "quantize_x: n must be whole groups of 32");
+  const int64_t warps = (int64_t)(n / 32) * count;
+  quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride);
+  B200_LAUNCHED("quantize_kernel");
+  return 0;
+}
+
+int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
+                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
+  const int64_t warps = (int64_t)(n / 32) * count;
+  swiglu_quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq, q_stride, xs,
+                                                                   s_stride);
+  B200_LAUNCHED("swiglu_quantize_kernel");
+  return 0;
+}
+
+int launch_embed(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim, float *x,
+                 int64_t x_stride, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  embed_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(w, s, group, tokens, count, dim, x,
+                                                                          x_stride);
+  B200_LAUNCHED("embed_kernel");
+  return 0;
+}
+
+int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v, int64_t kv_stride, const float *cos,
+                      const float *sin, const int32_t *pos, const int32_t *seq, int count, void *kc, void *vc,
+                      int64_t seq_stride, int half, int nh, int nkv, int hs, int rot, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (hs % 2) return fail(B200FWD_EINVAL, "rope: the head size must be even");
+  const int total = (nh + nkv) * (hs / 2) + nkv * hs;
+  dim3 grid(blocks_for(total, 256), count);
+  rope_cache_kernel<<<grid, 256, 0, stream>>>(q, q_stride, k, v, kv_stride, cos, sin, pos, seq,
+                                              reinterpret_cast<uint8_t *>(kc), reinterpret_cast<uint8_t *>(vc),
+                                              seq_stride, half, nh, nkv, hs, rot);
+  B200_LAUNCHED("rope_cache_kernel");
+  return 0;
+}
+
+int prepare_attention() {
+  int device = 0;
+  B200_CUDA(cudaGetDevice(&device));
+  static std::atomic<uint64_t> opted{0};
+  if (device >= 64 || !(opted.load() & (1ull << device))) {
+    B200_CUDA(cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SOFTMAX_SMEM));
+    if (device < 64) opted.fetch_or(1ull << device);
+  }
+  return 0;
+}
+
+int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
+                     float *att, const int32_t *seq, const int32_t *pos, int pos0, int count, int64_t seq_stride,
+                     int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int half, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (nkv <= 0 || nh % nkv) return fail(B200FWD_EINVAL, "attention: heads must be a multiple of the kv heads");
+  if (max_count > P) return fail(B200FWD_EINVAL, "attention: a position past the scratch");
+  const int G = nh / nkv;
+  const int chunks = (max_count + ATTN_CHUNK - 1) / ATTN_CHUNK;
+  const size_t smem_scores = (size_t)(G * hs) * sizeof(float);
+  dim3 g1(chunks, nkv, count);
+  if (half)
+    attn_scores_kernel<true><<<g1, ATTN_CHUNK, smem_scores, stream>>>(q, q_stride, kc, att, seq, pos, pos0,
+                                                                       seq_stride, P, nh, nkv, hs, h0, h1);
+  else
+    attn_scores_kernel<false><<<g1, ATTN_CHUNK, smem_scores, stream>>>(q, q_stride, kc, att, seq, pos, pos0,
+                                                                        seq_stride, P, nh, nkv, hs, h0, h1);
+  B200_LAUNCHED("attn_scores_kernel");
+  const size_t smem_soft = (size_t)max_count * sizeof(float);
+  if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
+  CHECK_RC(prepare_attention());
+  attn_softmax_kernel<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
+  B200_LAUNCHED("attn_softmax_kernel");
+  const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
+  if (half)
+    attn_values_kernel<true><<<dim3(nkv, count), threads, 0, stream>>>(out, out_stride, vc, att, seq, pos, pos0,
+                                                                        seq_stride, P, nh, nkv, hs, h0, h1);
+  else
+    attn_values_kernel<false><<<dim3(nkv, count), threads, 0, stream>>>(out, out_stride, vc, att, seq, pos, pos0,
+                                                                         seq_stride, P, nh, nkv, hs, h0, h1);
+  B200_LAUNCHED("attn_values_kernel");
+  return 0;
+}
+
+int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps, int count, int64_t stride,
+                   cudaStream_t stream) {
+  if (count <= 0) return 0;
+  rmsnorm_kernel<<<count, 256, 0, stream>>>(out, x, w, n, eps, stride);
+  B200_LAUNCHED("rmsnorm_kernel");
+  return 0;
+}
+
+int launch_rope(float *v, const float *fcr, const float *fci, int nh, int hs, int rot, cudaStream_t stream) {
+  const int turned = rot > 0 && rot < hs ? rot : hs;
+  const int pairs = nh * (turned / 2);
+  if (pairs <= 0) return 0;
+  rope_kernel<<<blocks_for(pairs, 128), 128, 0, stream>>>(v, fcr, fci, nh, hs, rot);
+  B200_LAUNCHED("rope_kernel");
+  return 0;
+}
+
+int launch_add_columns(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride, int nc,
+                       int n, int count, cudaStream_t stream) {
+  if (count <= 0 || nc <= 0) return 0;
+  add_columns_kernel<<<blocks_for((int64_t)n * count, 256), 256, 0, stream>>>(y, y_stride, rows, a, a_stride, nc, n,
+                                                                             count);
+  B200_LAUNCHED("add_columns_kernel");
+  return 0;
+}
+
+int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count, int mode, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  argmax_kernel<<<count, 1024, 0, stream>>>(out, x, stride, n, mode);
+  B200_LAUNCHED("argmax_kernel");
+  return 0;
+}
+
+int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t src_stride, const int32_t *idx,
+                       int count, int dim, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  gather_rows_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(dst, dst_stride, src, src_stride,
+                                                                                idx, count, dim);
+  B200_LAUNCHED("gather_rows_kernel");
+  return 0;
+}
+
+int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+                           const int32_t *channels, int nch, cudaStream_t stream) {
+  if (nch <= 0) return 0;
+  outlier_columns_kernel<<<blocks_for((int64_t)vocab * nch, 256), 256, 0, stream>>>(cols, w, s, group, dim, vocab,
+                                                                                     channels, nch);
+  B200_LAUNCHED("outlier_columns_kernel");
+  return 0;
+}
+
+int launch_to_f16(uint16_t *out, const float *x, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  to_f16_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, x, n);
+  B200_LAUNCHED("to_f16_kernel");
+  return 0;
+}
+int launch_from_f16(float *out, const uint16_t *x, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  from_f16_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, x, n);
+  B200_LAUNCHED("from_f16_kernel");
+  return 0;
+}
+int launch_add_inplace(float *x, const float *y, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  add_inplace_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(x, y, n);
+  B200_LAUNCHED("add_inplace_kernel");
+  return 0;
+}
+int launch_swiglu(float *out, const float *h1, const float *h3, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  swiglu_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, h1, h3, n);
+  B200_LAUNCHED("swiglu_kernel");
+  return 0;
+}
+int launch_int8_sums(int32_t *out, const int8_t *w, int64_t groups, cudaStream_t stream) {
+  if (groups <= 0) return 0;
+  int8_sums_kernel<<<blocks_for(groups, 256), 256, 0, stream>>>(out, w, groups);
+  B200_LAUNCHED("int8_sums_kernel");
+  return 0;
+}
+int launch_advance(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps, int32_t *step,
+                   int count, const float *logits, int64_t vocab, int32_t *bad, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (count > 1024) return fail(B200FWD_EINVAL, "advance: more than 1024 sequences");
+  advance_kernel<<<1, ((count + 31) / 32) * 32, 0, stream>>>(tokens, pos, ids, history, steps, step, count, logits,
+                                                             vocab, bad);
+  B200_LAUNCHED("advance_kernel");
+  return 0;
+}
+
+}  // namespace b200

@@ -1,0 +1,89 @@
+// kernels.h — the launchers of the hot-path kernels (kernels.cu), for the engine and the C ABI.
+//
+// Every launcher computes the reference's numbers to the bit (exact.cuh) and returns 0 or a B200FWD_E* code.
+// Token rows sit `*_stride` elements apart; all pointers are device pointers.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+// up to three matrices that read the same activations (q, k and v; w1 and w3), run as one launch: forward.js puts
+// them in one phase (forward.js:476,516). Rows of the jobs follow each other.
+struct MatJob {
+  const int8_t *w;    // [rows][n]
+  const float *s;     // [rows][n/32]
+  const int32_t *c;   // int8_sums corrections [rows][n/32], or null: dot(w, q - 64) taken directly
+  float *out;         // token t's row at out + t * out_stride
+  int rows;
+  int accumulate;     // out += the result (the residual add of forward.js:500,519), else out = the result
+  int64_t out_stride;
+};
+struct MatJobs {
+  MatJob job[3];
+  int njobs;
+  int n;
+  int total_rows;
+};
+
+// kernel_relaxed.ts:34-67/164-183 (relaxed) or kernel.ts:231-251 (8-bit): count tokens of activations
+int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_t q_stride, int64_t s_stride,
+                  int count, bool relaxed, cudaStream_t stream);
+
+// kernel.ts:330-342 rmsnorm then kernel.ts:129-156 quantize_x of its output, per token; channels (nch of them,
+// device) are taken out of the normalized vector first (forward.js:525-528: picked[c] = value, value = 0).
+// out_f (nullable) also gets the normalized floats.
+int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
+                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
+                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream);
+// kernel.ts:129-156 quantize_x, per token
+int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
+                    float *xs, int64_t s_stride, cudaStream_t stream);
+// kernel.ts:654-667 swiglu then quantize_x of its output, per token
+int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
+                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream);
+// forward.js:403-414 embed of int8 rows: x[t][i] = w[token*dim+i] * s[(token*dim+i)/group]; tokens on the device
+int launch_embed(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim, float *x,
+                 int64_t x_stride, cudaStream_t stream);
+// forward.js:489-494: rope (kernel.ts:344-357) on q and k of each token at its position, and k, v into its
+// sequence's cache (to_f16 when half). cache of sequence s: kc + s * seq_stride elements, [pos][nkv*hs]
+int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v, int64_t kv_stride, const float *cos,
+                      const float *sin, const int32_t *pos, const int32_t *seq, int count, void *kc, void *vc,
+                      int64_t seq_stride, int half, int nh, int nkv, int hs, int rot, cudaStream_t stream);
+// kernel.ts:447-566 attentionOf for count tokens, each against its sequence's cache up to its position (device
+// arrays seq and pos; or, with pos null, every token at pos0 of sequence 0). att: [count][nh][P] scratch
+// (P >= max position + 1), left holding the softmax weights; max_count bounds pos + 1 for the grid. Heads h0..h1.
+int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
+                     float *att, const int32_t *seq, const int32_t *pos, int pos0, int count, int64_t seq_stride,
+                     int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int half, cudaStream_t stream);
+constexpr int ATTN_CHUNK = 128;
+// the attention kernels' shared-memory opt-in on the current device (once; before any graph capture)
+int prepare_attention();
+// kernel.ts:671-689 add_columns for count tokens (y rows y_stride apart, a rows a_stride apart)
+int launch_add_columns(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride, int nc,
+                       int n, int count, cudaStream_t stream);
+// argmax of count rows: mode 0 kernel.ts:695-699 (first index with `>`), mode 1 numpy.argmax (a NaN wins)
+int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count, int mode, cudaStream_t stream);
+// dst[i] = src[idx[i]] (rows of dim floats)
+int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t src_stride, const int32_t *idx,
+                       int count, int dim, cudaStream_t stream);
+// forward.js:799-813 the outlier channels' float32 columns: cols[i][v] = w[v*dim+c_i] * s[v*groups + c_i/group]
+int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+                           const int32_t *channels, int nch, cudaStream_t stream);
+int launch_to_f16(uint16_t *out, const float *x, int64_t n, cudaStream_t stream);
+int launch_from_f16(float *out, const uint16_t *x, int64_t n, cudaStream_t stream);
+int launch_add_inplace(float *x, const float *y, int64_t n, cudaStream_t stream);
+int launch_swiglu(float *out, const float *h1, const float *h3, int64_t n, cudaStream_t stream);
+int launch_int8_sums(int32_t *out, const int8_t *w, int64_t groups, cudaStream_t stream);
+// greedy bookkeeping on the device: tokens[i] = ids[i]; pos[i] += 1; history[i * steps + *step] = ids[i]; ++*step;
+// *bad = 1 where the chosen logit (logits[i * vocab + id]) is not finite
+int launch_advance(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps, int32_t *step,
+                   int count, const float *logits, int64_t vocab, int32_t *bad, cudaStream_t stream);
+// kernel.ts:330-342 rmsnorm of count rows (stride floats apart)
+int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps, int count, int64_t stride,
+                   cudaStream_t stream);
+// kernel.ts:344-357 rope of one vector
+int launch_rope(float *v, const float *fcr, const float *fci, int nh, int hs, int rot, cudaStream_t stream);
+
+}  // namespace b200

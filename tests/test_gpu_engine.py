@@ -1,0 +1,202 @@
+"""The engine (include/b200fwd.h b200fwd_*) against the oracle's forward.js run(), to the bit, through the
+reference's engine interface. GPU only."""
+import hashlib
+import json
+
+import numpy as np
+import pytest
+
+import oracle
+from b200fwd import abi, checkpoint as ck
+from b200fwd.forward import Engine, external
+from conftest import GOLDEN
+from gpu_util import bits
+
+pytestmark = pytest.mark.gpu
+
+
+def golden_model(name):
+    g = np.load(GOLDEN / f"numpy_{name}.npz")
+    header = tuple(int(v) for v in g["header"])
+    data = ck.synthetic_checkpoint(header, seed=int(g["seed"]), norm=str(g["norm"]))
+    assert hashlib.sha256(data).digest() == g["sha256"].tobytes()
+    plan = json.loads((GOLDEN / f"plan_{name}.json").read_text())
+    d = np.load(GOLDEN / f"plan_{name}.npz")
+    plan["derived"] = {k: d[k].tobytes() for k in d.files}
+    return data, plan, g
+
+
+MODELS = ["tiny_gqa", "tiny_mha", "tiny_mqa"]
+
+
+@pytest.mark.parametrize("name", MODELS)
+@pytest.mark.parametrize("half_keys", [True, False])
+def test_forward_bit_identical_to_oracle(name, half_keys):
+    """forward() at every position of the NumPy engine's greedy text: the logits of the oracle's run(), to the bit,
+    over a cache that grows from 16 positions; keysAndValues the oracle's."""
+    data, plan, g = golden_model(name)
+    plan = dict(plan, kv_start=16)
+    eng = Engine(data, plan, half_keys=half_keys)
+    ref = oracle.OracleEngine(data, plan, half_keys=1 if half_keys else 0, threads=2)
+    assert ("float16" in eng.backend) == (half_keys and plan["half_kv"])
+    logits = np.zeros(plan["vocab_size"], np.float32)
+    eng.bind(logits)
+    tokens = g["tokens"]
+    for pos in range(len(tokens)):
+        eng.forward(int(tokens[pos]), pos)
+        want = ref.forward(int(tokens[pos]), pos)
+        assert np.array_equal(bits(logits), bits(want)), pos
+    kv = eng.keysAndValues(0, len(tokens))
+    rk, rv = ref.keys_values(0, len(tokens))
+    assert np.array_equal(bits(kv["keys"]), bits(rk)) and np.array_equal(bits(kv["values"]), bits(rv))
+    eng.release()
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_forward_many_blocks_are_tokens(name):
+    """tests/forward-check.mjs:440-451: the prompt in blocks of 37 (and of the engine's own block) is bit-identical
+    to token by token."""
+    data, plan, g = golden_model(name)
+    plan = dict(plan, kv_start=16)
+    tokens = [int(t) for t in g["tokens"]]
+    one = Engine(data, plan)
+    for pos, t in enumerate(tokens[:-1]):
+        one.forward(t, pos, False)
+    one.forward(tokens[-1], len(tokens) - 1)
+    a = one.logits()
+    blocks = Engine(data, plan)
+    for start in range(0, len(tokens) - 1, 37):
+        blocks.forwardMany(tokens[start:min(start + 37, len(tokens) - 1)], start)
+    blocks.forward(tokens[-1], len(tokens) - 1)
+    b = blocks.logits()
+    whole = Engine(data, plan, max_tokens=64)
+    whole.forwardMany(tokens[:-1], 0)
+    whole.forward(tokens[-1], len(tokens) - 1)
+    c = whole.logits()
+    assert np.array_equal(bits(a), bits(b)) and np.array_equal(bits(a), bits(c))
+
+
+def test_numpy_line_through_llama_style_driver():
+    """The engine against the reference's NumPy engine at forward.js's own line (tests/forward-check.mjs:437): the
+    most likely token the same at >= 85% of 128 positions, perplexity within 5%."""
+    for name in MODELS:
+        data, plan, g = golden_model(name)
+        ext = external(data)
+        eng = ext.start(plan)
+        logits = np.zeros(plan["vocab_size"], np.float32)
+        eng.bind(logits)
+        tokens, ref = g["tokens"], g["logits"]
+        same, nll, nll_ref = 0, 0.0, 0.0
+        for pos in range(len(tokens)):
+            eng.forward(int(tokens[pos]), pos, True)
+            same += int(np.argmax(logits) == np.argmax(ref[pos]))
+            if pos + 1 < len(tokens):
+                for lg, which in ((logits, 0), (ref[pos], 1)):
+                    x = lg.astype(np.float64)
+                    lp = x - x.max() - np.log(np.exp(x - x.max()).sum())
+                    if which == 0:
+                        nll -= lp[tokens[pos + 1]]
+                    else:
+                        nll_ref -= lp[tokens[pos + 1]]
+        assert same / len(tokens) >= 0.85, name
+        assert abs(np.exp((nll - nll_ref) / (len(tokens) - 1)) - 1) <= 0.05, name
+
+
+def stories_plan(data, seq_len=256):
+    return ck.make_plan(ck.header_of(data), lambda o, n: data[o:o + n])
+
+
+@pytest.fixture(scope="module")
+def stories():
+    """the stories15M shape, N(0, 0.02) weights (seed 0) quantized by quantize()."""
+    data = ck.synthetic_checkpoint(ck.STORIES15M, seed=0)
+    return data, stories_plan(data)
+
+
+def test_stories15m_greedy_identical(stories):
+    """64 seeded prompt tokens, then 128 greedy tokens: the ids and every step's logits the oracle's to the bit
+    (forward.js's float16 cache: stories15M is multi-head)."""
+    data, plan = stories
+    rng = np.random.default_rng(0)
+    prompt = [1] + [int(t) for t in rng.integers(0, 32000, 63)]
+    eng = Engine(data, plan)
+    ref = oracle.OracleEngine(data, plan, threads=4)
+    eng.forwardMany(prompt[:-1], 0)
+    ref.forward_many(prompt[:-1], 0)
+    logits = np.zeros(32000, np.float32)
+    eng.bind(logits)
+    token, ids, ref_ids = prompt[-1], [], []
+    rtoken = token
+    for pos in range(63, 63 + 128):
+        eng.forward(token, pos)
+        want = ref.forward(rtoken, pos)
+        assert np.array_equal(bits(logits), bits(want)), pos
+        token, rtoken = int(np.argmax(logits)), int(np.argmax(want))
+        ids.append(token)
+        ref_ids.append(rtoken)
+    assert ids == ref_ids
+
+
+def test_slots_are_independent(stories):
+    """The batched extension: three sequences in one run, token by token and in prompt blocks, each bit-identical
+    to the same sequence alone; generate_greedy on the device gives run()'s argmax ids."""
+    data, plan = stories
+    rng = np.random.default_rng(1)
+    prompts = [[1] + [int(t) for t in rng.integers(0, 32000, n)] for n in (20, 33, 7)]
+    alone = []
+    for p in prompts:
+        e = Engine(data, plan)
+        e.forwardMany(p[:-1], 0)
+        e.forward(p[-1], len(p) - 1)
+        alone.append(e.logits())
+        e.release()
+    eng = Engine(data, plan, slots=3)
+    # the prompts in one run (every slot's tokens in order), then the last tokens together
+    slots = np.concatenate([[i] * (len(p) - 1) for i, p in enumerate(prompts)])
+    toks = np.concatenate([p[:-1] for p in prompts])
+    pos = np.concatenate([np.arange(len(p) - 1) for p in prompts])
+    eng.run(slots, toks, pos)
+    last, am = eng.run([0, 1, 2], [p[-1] for p in prompts], [len(p) - 1 for p in prompts], want=[1, 1, 1])
+    for i in range(3):
+        assert np.array_equal(bits(last[i]), bits(alone[i])), i
+        assert am[i] == int(np.argmax(alone[i]))
+    # 12 greedy steps on the device from there, against run() step by step on a second engine
+    first = [int(a) for a in am]
+    p0 = [len(p) for p in prompts]
+    ids = eng.generate_greedy([0, 1, 2], first, p0, 12)
+    other = Engine(data, plan, slots=3)
+    other.run(slots, toks, pos)
+    other.run([0, 1, 2], [p[-1] for p in prompts], [len(p) - 1 for p in prompts])
+    cur, steps = list(first), []
+    for s in range(12):
+        _, am2 = other.run([0, 1, 2], cur, [p + s for p in p0], want=[1, 1, 1], logits=False)
+        steps.append(list(am2))
+        cur = [int(a) for a in am2]
+    assert np.array_equal(ids, np.array(steps).T)
+
+
+def test_errors_are_raised_not_crashed(stories):
+    data, plan = stories
+    eng = Engine(data, plan)
+    with pytest.raises(abi.EngineError, match="vocabulary"):
+        eng.forward(32000, 0)
+    with pytest.raises(abi.EngineError, match="context"):
+        eng.forward(5, 256)
+    bad = dict(plan, dim=320)
+    with pytest.raises(abi.EngineError):
+        Engine(data, bad)
+
+
+def test_not_finite_logits_stop_greedy(stories):
+    """llama2_numpy.greedy's NOT_FINITE (public/llama2_numpy.py:1521-1527): a classifier whose scales are NaN
+    gives logits that are no numbers; generate_greedy says so, and the engine is still usable."""
+    data, plan = stories
+    broken = bytearray(data)
+    t = plan["tensors"]["token_embedding_table"]
+    nan = np.full(32000 * 288 // 32, np.nan, np.float32).tobytes()
+    broken[t["scales"]:t["scales"] + len(nan)] = nan
+    eng = Engine(bytes(broken), plan)
+    with pytest.raises(abi.EngineError) as err:
+        eng.generate_greedy([0], [1], [0], 2)
+    assert err.value.code == abi.ENOTFINITE
+    eng.forward(1, 0)  # still answers

@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cstring>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -492,7 +493,8 @@ float oracle_vexp(float x) { return vexp(x); }
 // ------------------------------------------------------------------------------------------- the layer loop
 namespace {
 
-// public/jobs.js + helper.js: a persistent pool; a phase's jobs are cut into chunks taken from an atomic counter
+// public/jobs.js + helper.js: a persistent pool; a phase's jobs are cut into chunks taken from an atomic counter.
+// Each phase has its own counters, so a helper that wakes late only ever takes chunks of the phase it saw.
 class Pool {
  public:
   explicit Pool(int threads) : threads_(std::max(1, threads)) {
@@ -514,26 +516,31 @@ class Pool {
       for (int c = 0; c < total; c++) body(c);
       return;
     }
+    auto phase = std::make_shared<Phase>();
+    phase->body = &body;
+    phase->total = total;
     {
       std::lock_guard<std::mutex> g(m_);
-      body_ = &body;
-      total_ = total;
-      next_.store(0);
-      done_.store(0);
+      current_ = phase;
       gen_++;
     }
     cv_.notify_all();
-    work();
+    work(*phase);
     std::unique_lock<std::mutex> g(m_);
-    done_cv_.wait(g, [&] { return done_.load() == total_; });
-    body_ = nullptr;
+    done_cv_.wait(g, [&] { return phase->done.load() == phase->total; });
+    current_.reset();
   }
 
  private:
-  void work() {
-    for (int c = next_.fetch_add(1); c < total_; c = next_.fetch_add(1)) {
-      (*body_)(c);
-      if (done_.fetch_add(1) + 1 == total_) {
+  struct Phase {
+    const std::function<void(int)> *body = nullptr;
+    int total = 0;
+    std::atomic<int> next{0}, done{0};
+  };
+  void work(Phase &p) {
+    for (int c = p.next.fetch_add(1); c < p.total; c = p.next.fetch_add(1)) {
+      (*p.body)(c);
+      if (p.done.fetch_add(1) + 1 == p.total) {
         std::lock_guard<std::mutex> g(m_);
         done_cv_.notify_all();
       }
@@ -542,23 +549,22 @@ class Pool {
   void loop() {
     uint64_t seen = 0;
     for (;;) {
+      std::shared_ptr<Phase> phase;
       {
         std::unique_lock<std::mutex> g(m_);
         cv_.wait(g, [&] { return gen_ != seen; });
         seen = gen_;
         if (quit_) return;
-        if (!body_) continue;
+        phase = current_;
       }
-      work();
+      if (phase) work(*phase);
     }
   }
   int threads_;
   std::vector<std::thread> workers_;
   std::mutex m_;
   std::condition_variable cv_, done_cv_;
-  const std::function<void(int)> *body_ = nullptr;
-  int total_ = 0;
-  std::atomic<int> next_{0}, done_{0};
+  std::shared_ptr<Phase> current_;
   uint64_t gen_ = 0;
   bool quit_ = false;
 };

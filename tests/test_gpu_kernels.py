@@ -46,8 +46,8 @@ def mm():
 
 def test_int8_sums(lib):
     w, want = F.int8_sums_case()
-    out = empty(want.size, np.int32)
-    abi.check(lib.b200k_int8_sums(ptr(out), ptr(dev(w)), want.size, None))
+    out, dw = empty(want.size, np.int32), dev(w)
+    abi.check(lib.b200k_int8_sums(ptr(out), ptr(dw), want.size, None))
     assert np.array_equal(host(out), want)
 
 
@@ -119,8 +119,8 @@ def test_quantize_x(lib):
     x[2, 32:64] = 1e-39       # subnormal amax: the inverse overflows (T136)
     x[3, 64:96] = -5.0        # all the same value
     for bias in (0, 64):
-        dq, ds = empty((count, n), np.int8), empty((count, n // 32), np.float32)
-        abi.check(lib.b200k_quantize_x(ptr(dq), ptr(ds), ptr(dev(x)), n, bias, count, n, n, n // 32, None))
+        dq, ds, dx = empty((count, n), np.int8), empty((count, n // 32), np.float32), dev(x)
+        abi.check(lib.b200k_quantize_x(ptr(dq), ptr(ds), ptr(dx), n, bias, count, n, n, n // 32, None))
         gq, gs = host(dq), host(ds)
         for t in range(count):
             wq, wss = oracle.quantize_x(x[t], bias)
@@ -132,7 +132,8 @@ def attention_gpu(lib, q, kc, vc, pos, nh, nkv, hs, half, h0=0, h1=None):
     h1 = nh if h1 is None else h1
     out = full(nh * hs, float("nan"))
     att = full(nh * (pos + 1), 0.0)
-    abi.check(lib.b200k_attention(ptr(out), ptr(dev(q)), ptr(dev(kc)), ptr(dev(vc)), ptr(att), pos, nh, nkv, hs, h0, h1,
+    dq, dk, dv = dev(q), dev(kc), dev(vc)  # held until the kernel has run
+    abi.check(lib.b200k_attention(ptr(out), ptr(dq), ptr(dk), ptr(dv), ptr(att), pos, nh, nkv, hs, h0, h1,
                                   1 if half else 0, None))
     return host(out), host(att)
 
@@ -192,8 +193,10 @@ def test_attention_batch_is_per_token(lib):
     q = rng.standard_normal((5, nh * hs)).astype(np.float32)
     out = full((5, nh * hs), float("nan"))
     att = full((5, nh, P), 0.0)
-    abi.check(lib.b200k_attention_batch(ptr(out), ptr(dev(q)), ptr(dev(kc)), ptr(dev(vc)), ptr(att), ptr(dev(seq)),
-                                        ptr(dev(pos)), 5, P * kvd, P, nh, nkv, hs, 1, None))
+    held = [dev(a) for a in (q, kc, vc, seq, pos)]
+    dq, dk, dv, dseq, dpos = held
+    abi.check(lib.b200k_attention_batch(ptr(out), ptr(dq), ptr(dk), ptr(dv), ptr(att), ptr(dseq), ptr(dpos), 5,
+                                        P * kvd, P, nh, nkv, hs, 1, None))
     got = host(out)
     for i in range(5):
         ref, _ = oracle.attention(q[i], kc[seq[i]], vc[seq[i]], int(pos[i]), nh, nkv, hs, half=True)
@@ -202,15 +205,15 @@ def test_attention_batch_is_per_token(lib):
 
 def test_f16_conversions(lib):
     halves = np.arange(65536, dtype=np.uint32).astype(np.uint16)
-    out = empty(65536, np.float32)
-    abi.check(lib.b200k_from_f16(ptr(out), ptr(dev(halves)), 65536, None))
+    out, dh = empty(65536, np.float32), dev(halves)
+    abi.check(lib.b200k_from_f16(ptr(out), ptr(dh), 65536, None))
     assert np.array_equal(bits(host(out)), bits(oracle.from_f16(halves)))
     rng = np.random.default_rng(0)
     x = np.concatenate([rng.standard_normal(50000).astype(np.float32) * np.float32(10) ** rng.integers(-9, 6, 50000),
                         np.float32([0, -0.0, 65504, 65519, 65520, 1e6, 6e-8, 3e-8, 2.9e-8, np.inf, -np.inf])])
     x = x.astype(np.float32)
-    h = empty(x.size, np.uint16)
-    abi.check(lib.b200k_to_f16(ptr(h), ptr(dev(x)), x.size, None))
+    h, dx = empty(x.size, np.uint16), dev(x)
+    abi.check(lib.b200k_to_f16(ptr(h), ptr(dx), x.size, None))
     assert np.array_equal(host(h).view(np.uint16), oracle.to_f16(x))
 
 
@@ -219,36 +222,36 @@ def test_small_kernels(lib):
     n = 1003
     h1 = (rng.standard_normal(n) * 40).astype(np.float32)
     h3 = rng.standard_normal(n).astype(np.float32)
-    out = empty(n, np.float32)
-    abi.check(lib.b200k_swiglu(ptr(out), ptr(dev(h1)), ptr(dev(h3)), n, None))
+    out, d1, d3 = empty(n, np.float32), dev(h1), dev(h3)
+    abi.check(lib.b200k_swiglu(ptr(out), ptr(d1), ptr(d3), n, None))
     assert np.array_equal(bits(host(out)), bits(oracle.swiglu(h1, h3)))
     for dim in (288, 4096, 99):
         x = rng.standard_normal((3, dim)).astype(np.float32)
         w = rng.standard_normal(dim).astype(np.float32)
-        o = empty((3, dim), np.float32)
-        abi.check(lib.b200k_rmsnorm(ptr(o), ptr(dev(x)), ptr(dev(w)), dim, np.float32(1e-5), 3, dim, None))
+        o, dx, dw = empty((3, dim), np.float32), dev(x), dev(w)
+        abi.check(lib.b200k_rmsnorm(ptr(o), ptr(dx), ptr(dw), dim, np.float32(1e-5), 3, dim, None))
         g = host(o)
         for t in range(3):
             assert np.array_equal(bits(g[t]), bits(oracle.rmsnorm(x[t], w))), (dim, t)
     v = rng.standard_normal(6 * 48).astype(np.float32)
     c, s = rng.standard_normal(24).astype(np.float32), rng.standard_normal(24).astype(np.float32)
     for rot in (0, 16):
-        dv = dev(v)
-        abi.check(lib.b200k_rope(ptr(dv), ptr(dev(c)), ptr(dev(s)), 6, 48, rot, None))
+        dv, dc, ds = dev(v), dev(c), dev(s)
+        abi.check(lib.b200k_rope(ptr(dv), ptr(dc), ptr(ds), 6, 48, rot, None))
         assert np.array_equal(bits(host(dv)), bits(oracle.rope(v, c, s, 6, 48, rot)))
     y = rng.standard_normal(32000).astype(np.float32)
     rows = rng.standard_normal((8, 32000)).astype(np.float32)
     a = rng.standard_normal(8).astype(np.float32)
-    dy = dev(y)
-    abi.check(lib.b200k_add_columns(ptr(dy), ptr(dev(rows)), ptr(dev(a)), 8, 32000, None))
+    dy, drows, da = dev(y), dev(rows), dev(a)
+    abi.check(lib.b200k_add_columns(ptr(dy), ptr(drows), ptr(da), 8, 32000, None))
     assert np.array_equal(bits(host(dy)), bits(oracle.add_columns(y, rows, a)))
     xx, yy = rng.standard_normal(777).astype(np.float32), rng.standard_normal(777).astype(np.float32)
-    dx = dev(xx)
-    abi.check(lib.b200k_add_inplace(ptr(dx), ptr(dev(yy)), 777, None))
+    dx, dyy = dev(xx), dev(yy)
+    abi.check(lib.b200k_add_inplace(ptr(dx), ptr(dyy), 777, None))
     assert np.array_equal(bits(host(dx)), bits(xx + yy))
     for z in (rng.standard_normal(128256).astype(np.float32), np.float32([1, 5, 5, 2]), np.float32([np.nan, 1, 2])):
-        r = empty(1, np.int32)
-        abi.check(lib.b200k_argmax(ptr(r), ptr(dev(z)), z.size, None))
+        r, dz = empty(1, np.int32), dev(z)
+        abi.check(lib.b200k_argmax(ptr(r), ptr(dz), z.size, None))
         assert host(r)[0] == oracle.argmax(z)
 
 

@@ -82,10 +82,10 @@ typedef struct b200fwd_options {
                           203 `halfKeys ?? kvHeads >= heads`); 0: float32; 1: float16 (keysInHalf said so) */
   int32_t slots;       /* independent sequences the engine holds (1 = forward.js; >1 = the batched extension) */
   int32_t device;      /* CUDA device ordinal */
-  int32_t max_tokens;  /* the most tokens one run() takes (a prompt block times slots); 0 = 16 * slots */
+  int32_t max_tokens;  /* the most tokens one run() takes (a prompt block times slots); 0 = max(512, 16 * slots) */
   int32_t capacity;    /* first KV capacity per slot; 0 = plan.kv_start (then doubled as forward.js grow()) */
-  int32_t checkpoint_on_device; /* 1: `checkpoint` is a DEVICE pointer the caller keeps alive until destroy (the
-                                   engine reads the tensors in place, no copy); 0: host memory, copied to HBM */
+  int32_t checkpoint_on_device; /* 1: `checkpoint` is a DEVICE pointer, whose tensors create() copies into the
+                                   engine's own layout (the caller may free it afterwards); 0: host memory */
   int32_t reserved[6];
 } b200fwd_options;
 
@@ -167,6 +167,13 @@ int b200k_int8_sums(int32_t *out, const int8_t *w, int64_t groups, b200fwd_strea
 int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
                      const int32_t *wc, int32_t n, int32_t r0, int32_t r1, int32_t count, int64_t out_stride,
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream);
+/* kernel_relaxed.ts:34-67 / 164-183 on activations already less the bias (xq[i] = q[i] - 64, signed; the engine
+ * keeps them so): all `rows` rows of W for `count` tokens, the same numbers to the bit. From 16 tokens on (with
+ * n >= 128 and rows >= 128) it runs on the tensor cores (tcgen05.mma kind::i8, one MMA per group of 32), below on
+ * the CUDA cores. xq and wq 16-byte aligned, q_stride a multiple of 16. */
+int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
+                     int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
+                     b200fwd_stream stream);
 /* kernel.ts:231-258 matmul_q8: the same on quantize_x(bias 0) activations, lane order of dot32. */
 int b200k_matmul_q8(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
                     int32_t r0, int32_t r1, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,

@@ -3,7 +3,13 @@
 #include <string>
 
 #include "common.h"
+#include "gemm_tc.h"
 #include "kernels.h"
+
+namespace {
+// the tensor-core kernel's wait-gave-up word for the kernel entry points
+__device__ int capi_tc_error;
+}  // namespace
 
 using namespace b200;
 
@@ -58,6 +64,60 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream) {
   return guarded([&] {
     return matmul(xout, xq, xs, wq, ws, wc, n, r0, r1, count, out_stride, q_stride, s_stride, true, stream);
+  });
+}
+
+int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
+                     int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
+                     b200fwd_stream stream) {
+  return guarded([&] {
+    if (!xout || !xq || !xs || !wq || !ws) return fail(B200FWD_EINVAL, "matmul_q8s: null pointer");
+    if (n <= 0 || n % 32 || rows < 0 || count < 0) return fail(B200FWD_EINVAL, "matmul_q8s: bad sizes");
+    if (rows == 0 || count == 0) return 0;
+    if (q_stride % 16 || (reinterpret_cast<uintptr_t>(xq) % 16) || (reinterpret_cast<uintptr_t>(wq) % 16))
+      return fail(B200FWD_EINVAL, "matmul_q8s: weights and activations must be 16-byte aligned");
+    cudaStream_t st = as_stream(stream);
+    if (count < 16 || n < 128 || rows < 128) {
+      MatJobs jobs{};
+      jobs.job[0] = {wq, ws, nullptr, xout, rows, 0, out_stride};
+      jobs.njobs = 1;
+      jobs.n = n;
+      jobs.total_rows = rows;
+      jobs.signed_input = 1;
+      return launch_matvec(jobs, xq, xs, q_stride, s_stride, count, true, st);
+    }
+    int *err = nullptr;
+    B200_CUDA(cudaGetSymbolAddress((void **)&err, capi_tc_error));
+    const int row_tiles = (rows + 127) / 128;
+    int bn = 64;
+    while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
+    CUtensorMap wmap, xmap;
+    int rc = make_i8_map(&wmap, wq, n, rows, n, 128);
+    if (!rc) rc = make_i8_map(&xmap, xq, n, count, q_stride, bn);
+    if (rc) return rc;
+    GemmArgs a{};
+    a.ws = ws;
+    a.xs = xs;
+    a.out = xout;
+    a.error = err;
+    a.n = n;
+    a.rows = rows;
+    a.count = count;
+    a.w_row0 = 0;
+    a.s_stride = s_stride;
+    a.out_stride = out_stride;
+    a.accumulate = 0;
+    rc = launch_gemm_tc(wmap, xmap, a, bn, st);
+    if (rc) return rc;
+    int32_t e = 0;
+    B200_CUDA(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, st));
+    B200_CUDA(cudaStreamSynchronize(st));
+    if (e) {
+      const int32_t zero = 0;
+      B200_CUDA(cudaMemcpy(err, &zero, 4, cudaMemcpyHostToDevice));
+      return fail(B200FWD_ETIMEOUT, "matmul_q8s: a tensor-core pipeline wait gave up (code " + std::to_string(e) + ")");
+    }
+    return 0;
   });
 }
 

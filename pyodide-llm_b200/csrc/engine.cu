@@ -11,12 +11,14 @@
 // run() is forward.js run() (forward.js:452-531) over tokens that may belong to different slots.
 #include <algorithm>
 #include <cmath>
+#include <initializer_list>
 #include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "common.h"
+#include "gemm_tc.h"
 #include "kernels.h"
 
 namespace b200 {
@@ -40,10 +42,12 @@ int cuda_fail(cudaError_t e, const char *what) {
 
 namespace {
 
+// an int8 matrix of every layer (rows x n each), values then scales, and its TMA map over all layers' rows
 struct Matrix {
   int8_t *w = nullptr;
   float *s = nullptr;
   int rows = 0, n = 0, layers = 1;
+  CUtensorMap map;
   const int8_t *layer_w(int l) const { return w + (int64_t)l * rows * n; }
   const float *layer_s(int l) const { return s + (int64_t)l * rows * (n / 32); }
 };
@@ -70,7 +74,9 @@ struct b200fwd_engine {
   bool relaxed, half;
   int bias;
   float eps;
-  Matrix emb, wq, wk, wv, wo, w1, w2, w3, wcls;
+  // q, k and v of a layer as one matrix of qDim + 2 kvDim rows, w1 and w3 as one of 2 hidden rows (forward.js puts
+  // each set in one phase: forward.js:476,516)
+  Matrix emb, wqkv, wo, w13, w2, wcls;
   float *attW = nullptr, *ffnW = nullptr, *finalW = nullptr, *cosT = nullptr, *sinT = nullptr;
   int nch = 0;
   int32_t *channels = nullptr;
@@ -80,14 +86,17 @@ struct b200fwd_engine {
   uint8_t *cache = nullptr;
   // activations
   int T = 0;
-  float *x = nullptr, *xb = nullptr, *q = nullptr, *kn = nullptr, *vn = nullptr, *hb = nullptr, *hb2 = nullptr;
+  int QKV = 0;
+  float *x = nullptr, *xb = nullptr, *qkv = nullptr, *h13 = nullptr;
   float *att = nullptr;
   int8_t *xq = nullptr;
   float *xs = nullptr;
   float *xl = nullptr, *picked = nullptr, *logits = nullptr;
   int logit_rows = 0;
   int32_t *argmax = nullptr;
-  int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad
+  int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tensor-core error
+  CUtensorMap xmap[3];          // the activations for the tensor cores' tiles of 16, 32 and 64 tokens
+  bool tensor_cores = true;
   int32_t *meta_h = nullptr;    // pinned host copy
   int32_t *history = nullptr;   // greedy ids [slots][steps]
   int history_len = 0;
@@ -104,6 +113,7 @@ struct b200fwd_engine {
   int32_t *want_d() { return meta + 3 * T; }
   int32_t *step_d() { return meta + 4 * T; }
   int32_t *bad_d() { return meta + 4 * T + 1; }
+  int32_t *tc_error_d() { return meta + 4 * T + 2; }
   int esize() const { return half ? 2 : 4; }
   int64_t seq_stride() const { return (int64_t)layers * 2 * capacity * kvDim; }
   uint8_t *layer_keys(int l) { return cache + (int64_t)(l * 2) * capacity * kvDim * esize(); }
@@ -163,6 +173,46 @@ int upload_matrix(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_d
   return 0;
 }
 
+// several tensors of the same layers and row length as one matrix per layer, their rows one after another
+int upload_fused(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_device,
+                 std::initializer_list<std::pair<const b200fwd_tensor *, const char *>> parts, Matrix &m) {
+  m = Matrix();
+  int n = -1, layers = -1, rows = 0;
+  for (auto &pt : parts) {
+    const b200fwd_tensor &t = *pt.first;
+    if (t.kind != B200FWD_TENSOR_INT8)
+      return fail(B200FWD_EUNSUPPORTED, std::string("tensor ") + pt.second + " is not int8 (this engine runs int8 only)");
+    if (t.ndim != 3 || t.group != 32 || t.shape[2] % 32)
+      return fail(B200FWD_EUNSUPPORTED, std::string("tensor ") + pt.second + ": layers of rows of whole groups of 32");
+    if (n >= 0 && (t.shape[2] != n || t.shape[0] != layers))
+      return fail(B200FWD_EINVAL, std::string("tensor ") + pt.second + " does not match the others of its phase");
+    n = (int)t.shape[2];
+    layers = (int)t.shape[0];
+    const int64_t count = elements(t);
+    if (t.offset < 0 || t.scales < 0 || (size_t)(t.offset + count) > size || (size_t)(t.scales + count / 8) > size)
+      return fail(B200FWD_EINVAL, std::string("tensor ") + pt.second + " lies outside the checkpoint");
+    rows += (int)t.shape[1];
+  }
+  m.rows = rows;
+  m.n = n;
+  m.layers = layers;
+  const int64_t count = (int64_t)layers * rows * n;
+  CHECK(alloc(e, (void **)&m.w, count));
+  CHECK(alloc(e, (void **)&m.s, count / 32 * 4));
+  int at = 0;
+  for (auto &pt : parts) {
+    const b200fwd_tensor &t = *pt.first;
+    const int r = (int)t.shape[1];
+    B200_CUDA(cudaMemcpy2DAsync(m.w + (int64_t)at * n, (size_t)rows * n, ckpt + t.offset, (size_t)r * n, (size_t)r * n,
+                                layers, copy_kind(on_device), e->stream));
+    B200_CUDA(cudaMemcpy2DAsync(m.s + (int64_t)at * (n / 32), (size_t)rows * (n / 32) * 4, ckpt + t.scales,
+                                (size_t)r * (n / 32) * 4, (size_t)r * (n / 32) * 4, layers, copy_kind(on_device),
+                                e->stream));
+    at += r;
+  }
+  return 0;
+}
+
 int upload_floats(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_device, const b200fwd_tensor &t,
                   const char *name, int64_t want, float **out) {
   if (t.kind != B200FWD_TENSOR_F32)
@@ -181,19 +231,21 @@ int alloc_activations(b200fwd_engine *e) {
   const int T = e->T;
   CHECK(alloc(e, (void **)&e->x, (size_t)T * e->dim * 4));
   CHECK(alloc(e, (void **)&e->xb, (size_t)T * e->qDim * 4));
-  CHECK(alloc(e, (void **)&e->q, (size_t)T * e->qDim * 4));
-  CHECK(alloc(e, (void **)&e->kn, (size_t)T * e->kvDim * 4));
-  CHECK(alloc(e, (void **)&e->vn, (size_t)T * e->kvDim * 4));
-  CHECK(alloc(e, (void **)&e->hb, (size_t)T * e->hidden * 4));
-  CHECK(alloc(e, (void **)&e->hb2, (size_t)T * e->hidden * 4));
+  CHECK(alloc(e, (void **)&e->qkv, (size_t)T * e->QKV * 4));
+  CHECK(alloc(e, (void **)&e->h13, (size_t)T * 2 * e->hidden * 4));
   CHECK(alloc(e, (void **)&e->xq, (size_t)T * e->XQ));
   CHECK(alloc(e, (void **)&e->xs, (size_t)T * (e->XQ / 32) * 4));
   CHECK(alloc(e, (void **)&e->xl, (size_t)T * e->dim * 4));
   CHECK(alloc(e, (void **)&e->picked, (size_t)T * std::max(1, e->nch) * 4));
   CHECK(alloc(e, (void **)&e->argmax, (size_t)T * 4));
-  CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 2) * 4));
-  B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 2) * 4, e->stream));
-  B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 2) * 4));
+  CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 4) * 4));
+  B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 4) * 4, e->stream));
+  B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 4) * 4));
+  // the activations' TMA maps (rows of XQ bytes, one per token), for tiles of 16, 32 and 64 tokens
+  const int bns[3] = {16, 32, 64};
+  e->tensor_cores = e->tensor_cores && T >= 64 && e->XQ >= 128;
+  if (e->tensor_cores)
+    for (int i = 0; i < 3; i++) CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
   return 0;
 }
 
@@ -231,66 +283,85 @@ int grow(b200fwd_engine *e, int pos) {
   return 0;
 }
 
+// one matrix of one layer times the quantized activations of count tokens (in e->xq, less the bias): the tensor
+// cores from 16 tokens on (gemm_tc.cu), the CUDA cores below (kernels.cu); the same numbers either way
+int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t out_stride, int accumulate, int count) {
+  const int XS = e->XQ / 32;
+  // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 64 tokens: never past the tensors' extents)
+  if (count >= 16 && e->relaxed && e->tensor_cores && m.n >= 128 && (int64_t)m.layers * m.rows >= 128) {
+    GemmArgs a{};
+    a.ws = m.s;
+    a.xs = e->xs;
+    a.out = out;
+    a.error = e->tc_error_d();
+    a.n = m.n;
+    a.rows = m.rows;
+    a.count = count;
+    a.w_row0 = layer * m.rows;
+    a.s_stride = XS;
+    a.out_stride = out_stride;
+    a.accumulate = accumulate;
+    // the widest token tile that still gives every SM a tile
+    const int row_tiles = (m.rows + 127) / 128;
+    int bn = 64;
+    while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
+    const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
+    return launch_gemm_tc(m.map, e->xmap[which], a, bn, e->stream);
+  }
+  MatJobs jobs{};
+  jobs.job[0] = {m.layer_w(layer), m.layer_s(layer), nullptr, out, m.rows, accumulate, out_stride};
+  jobs.njobs = 1;
+  jobs.n = m.n;
+  jobs.total_rows = m.rows;
+  jobs.signed_input = 1;
+  return launch_matvec(jobs, e->xq, e->xs, e->XQ, XS, count, e->relaxed, e->stream);
+}
+
 // the layers over n tokens whose ids, slots and positions are in meta (device); the logits of the `want` tokens
 // (their indices in want_d) into logits rows 0..want-1, and their argmax. Enqueues only (graph-capturable).
 int forward_device(b200fwd_engine *e, int n, int want, int max_count) {
   cudaStream_t st = e->stream;
-  const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32;
+  const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32, QKV = e->QKV;
+  const int shift = e->bias;  // activations stored less the bias
+  float *q = e->qkv, *k = e->qkv + QD, *v = e->qkv + QD + KVD;
   CHECK(launch_embed(e->emb.w, e->emb.s, 32, e->tokens_d(), n, D, e->x, D, st));
   for (int l = 0; l < e->layers; l++) {
     CHECK(launch_norm_quantize(e->x, D, e->attW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
-                               nullptr, 0, nullptr, nullptr, 0, st));
-    MatJobs qkv{};
-    qkv.job[0] = {e->wq.layer_w(l), e->wq.layer_s(l), nullptr, e->q, e->wq.rows, 0, QD};
-    qkv.job[1] = {e->wk.layer_w(l), e->wk.layer_s(l), nullptr, e->kn, e->wk.rows, 0, KVD};
-    qkv.job[2] = {e->wv.layer_w(l), e->wv.layer_s(l), nullptr, e->vn, e->wv.rows, 0, KVD};
-    qkv.njobs = 3;
-    qkv.n = D;
-    qkv.total_rows = e->wq.rows + e->wk.rows + e->wv.rows;
-    CHECK(launch_matvec(qkv, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
-    CHECK(launch_rope_cache(e->q, QD, e->kn, e->vn, KVD, e->cosT, e->sinT, e->pos_d(), e->seq_d(), n,
-                            e->layer_keys(l), e->layer_values(l), e->seq_stride(), e->half ? 1 : 0, e->heads,
-                            e->kvHeads, e->hs, e->plan.rotary, st));
-    CHECK(launch_attention(e->xb, QD, e->q, QD, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(),
-                           0, n, e->seq_stride(), e->capacity, max_count, e->heads, e->kvHeads, e->hs, 0, e->heads,
+                               nullptr, 0, nullptr, nullptr, 0, st, shift));
+    CHECK(matmul(e, e->wqkv, l, e->qkv, QKV, 0, n));
+    CHECK(launch_rope_cache(q, QKV, k, v, QKV, e->cosT, e->sinT, e->pos_d(), e->seq_d(), n, e->layer_keys(l),
+                            e->layer_values(l), e->seq_stride(), e->half ? 1 : 0, e->heads, e->kvHeads, e->hs,
+                            e->plan.rotary, st));
+    CHECK(launch_attention(e->xb, QD, q, QKV, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(), 0,
+                           n, e->seq_stride(), e->capacity, max_count, e->heads, e->kvHeads, e->hs, 0, e->heads,
                            e->half ? 1 : 0, st));
-    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, XS, st));
-    MatJobs o{};
-    o.job[0] = {e->wo.layer_w(l), e->wo.layer_s(l), nullptr, e->x, e->wo.rows, 1, D};
-    o.njobs = 1;
-    o.n = QD;
-    o.total_rows = e->wo.rows;
-    CHECK(launch_matvec(o, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, XS, st, shift));
+    CHECK(matmul(e, e->wo, l, e->x, D, 1, n));
     CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
-                               nullptr, 0, nullptr, nullptr, 0, st));
-    MatJobs up{};
-    up.job[0] = {e->w1.layer_w(l), e->w1.layer_s(l), nullptr, e->hb, e->w1.rows, 0, HID};
-    up.job[1] = {e->w3.layer_w(l), e->w3.layer_s(l), nullptr, e->hb2, e->w3.rows, 0, HID};
-    up.njobs = 2;
-    up.n = D;
-    up.total_rows = e->w1.rows + e->w3.rows;
-    CHECK(launch_matvec(up, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
-    CHECK(launch_swiglu_quantize(e->hb, e->hb2, HID, HID, e->bias, n, e->xq, XQ, e->xs, XS, st));
-    MatJobs down{};
-    down.job[0] = {e->w2.layer_w(l), e->w2.layer_s(l), nullptr, e->x, e->w2.rows, 1, D};
-    down.njobs = 1;
-    down.n = HID;
-    down.total_rows = e->w2.rows;
-    CHECK(launch_matvec(down, e->xq, e->xs, XQ, XS, n, e->relaxed, st));
+                               nullptr, 0, nullptr, nullptr, 0, st, shift));
+    CHECK(matmul(e, e->w13, l, e->h13, 2 * HID, 0, n));
+    CHECK(launch_swiglu_quantize(e->h13, e->h13 + HID, 2 * HID, HID, e->bias, n, e->xq, XQ, e->xs, XS, st, shift));
+    CHECK(matmul(e, e->w2, l, e->x, D, 1, n));
   }
   if (want <= 0) return 0;
   // forward.js:521-530: the final norm of the wanted tokens, the outlier channels apart, the classifier, the columns
   CHECK(launch_gather_rows(e->xl, D, e->x, D, e->want_d(), want, D, st));
   CHECK(launch_norm_quantize(e->xl, D, e->finalW, D, e->eps, e->bias, want, e->xq, XQ, e->xs, XS, e->channels, e->nch,
-                             e->picked, nullptr, 0, st));
-  MatJobs cls{};
-  cls.job[0] = {e->wcls.layer_w(0), e->wcls.layer_s(0), nullptr, e->logits, e->wcls.rows, 0, (int64_t)e->vocab};
-  cls.njobs = 1;
-  cls.n = D;
-  cls.total_rows = e->wcls.rows;
-  CHECK(launch_matvec(cls, e->xq, e->xs, XQ, XS, want, e->relaxed, st));
+                             e->picked, nullptr, 0, st, shift));
+  CHECK(matmul(e, e->wcls, 0, e->logits, e->vocab, 0, want));
   CHECK(launch_add_columns(e->logits, e->vocab, e->columns, e->picked, e->nch, e->nch, e->vocab, want, st));
   CHECK(launch_argmax(e->argmax, e->logits, e->vocab, e->vocab, want, 1, st));
+  return 0;
+}
+
+// after a run: a tensor-core wait that gave up (it would leave the numbers unfinished) is an error
+int check_tc(b200fwd_engine *e) {
+  int32_t err = 0;
+  B200_CUDA(cudaMemcpy(&err, e->tc_error_d(), 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    B200_CUDA(cudaMemset(e->tc_error_d(), 0, 4));
+    return fail(B200FWD_ETIMEOUT, "a tensor-core pipeline wait gave up (code " + std::to_string(err) + ")");
+  }
   return 0;
 }
 
@@ -334,7 +405,7 @@ int run(b200fwd_engine *e, int n, const int32_t *slots, const int32_t *tokens, c
     if (argmax_out) B200_CUDA(cudaMemcpyAsync(argmax_out, e->argmax, (size_t)W * 4, cudaMemcpyDeviceToHost, e->stream));
   }
   B200_CUDA(cudaStreamSynchronize(e->stream));
-  return 0;
+  return check_tc(e);
 }
 
 int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, const b200fwd_options *options,
@@ -362,6 +433,7 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
   if (p.n_outliers < 0 || p.n_outliers > B200FWD_MAX_OUTLIERS) return fail(B200FWD_EINVAL, "bad outlier count");
   if (!p.freq_cis_real || !p.freq_cis_imag) return fail(B200FWD_EINVAL, "the plan has no RoPE tables");
   e->XQ = std::max(std::max(e->dim, e->hidden), e->qDim);
+  e->QKV = e->qDim + 2 * e->kvDim;
   e->relaxed = p.relaxed != 0;
   e->bias = e->relaxed ? 64 : 0;
   e->eps = p.rms_norm_eps;
@@ -376,26 +448,32 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
   B200_CUDA(cudaSetDevice(e->device));
   B200_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   CHECK(prepare_attention());
+  CHECK(prepare_gemm());
   const uint8_t *ck = (const uint8_t *)checkpoint;
   const bool dev = opt.checkpoint_on_device != 0;
   CHECK(upload_matrix(e, ck, size, dev, p.token_embedding_table, "token_embedding_table", e->emb));
-  CHECK(upload_matrix(e, ck, size, dev, p.wq, "wq", e->wq));
-  CHECK(upload_matrix(e, ck, size, dev, p.wk, "wk", e->wk));
-  CHECK(upload_matrix(e, ck, size, dev, p.wv, "wv", e->wv));
-  CHECK(upload_matrix(e, ck, size, dev, p.wo, "wo", e->wo));
-  CHECK(upload_matrix(e, ck, size, dev, p.w1, "w1", e->w1));
-  CHECK(upload_matrix(e, ck, size, dev, p.w2, "w2", e->w2));
-  CHECK(upload_matrix(e, ck, size, dev, p.w3, "w3", e->w3));
+  if (p.wq.shape[1] != e->qDim || p.wk.shape[1] != e->kvDim || p.wv.shape[1] != e->kvDim ||
+      p.w1.shape[1] != e->hidden || p.w3.shape[1] != e->hidden || p.wo.shape[2] != e->qDim ||
+      p.w2.shape[2] != e->hidden)
+    return fail(B200FWD_EINVAL, "a layer matrix's shape does not match the plan's sizes");
+  CHECK(upload_fused(e, ck, size, dev, {{&p.wq, "wq"}, {&p.wk, "wk"}, {&p.wv, "wv"}}, e->wqkv));
+  CHECK(upload_fused(e, ck, size, dev, {{&p.wo, "wo"}}, e->wo));
+  CHECK(upload_fused(e, ck, size, dev, {{&p.w1, "w1"}, {&p.w3, "w3"}}, e->w13));
+  CHECK(upload_fused(e, ck, size, dev, {{&p.w2, "w2"}}, e->w2));
   if (p.shared_classifier)
     e->wcls = e->emb;
   else
     CHECK(upload_matrix(e, ck, size, dev, p.wcls, "wcls", e->wcls));
-  const Matrix *shapes[] = {&e->wq, &e->wk, &e->wv, &e->wo, &e->w1, &e->w2, &e->w3};
-  const int want_rows[] = {e->qDim, e->kvDim, e->kvDim, e->dim, e->hidden, e->dim, e->hidden};
-  const int want_n[] = {e->dim, e->dim, e->dim, e->qDim, e->dim, e->hidden, e->dim};
-  for (int i = 0; i < 7; i++)
+  const Matrix *shapes[] = {&e->wqkv, &e->wo, &e->w13, &e->w2};
+  const int want_rows[] = {e->qDim + 2 * e->kvDim, e->dim, 2 * e->hidden, e->dim};
+  const int want_n[] = {e->dim, e->qDim, e->dim, e->hidden};
+  for (int i = 0; i < 4; i++)
     if (shapes[i]->rows != want_rows[i] || shapes[i]->n != want_n[i] || shapes[i]->layers != e->layers)
       return fail(B200FWD_EINVAL, "a layer matrix's shape does not match the plan's sizes");
+  Matrix *maps[] = {&e->wqkv, &e->wo, &e->w13, &e->w2, &e->wcls};
+  for (Matrix *m : maps)
+    if (m->n >= 128 && (int64_t)m->layers * m->rows >= 128)
+      CHECK(make_i8_map(&m->map, m->w, m->n, (int64_t)m->layers * m->rows, m->n, 128));
   if (e->emb.rows != e->vocab || e->emb.n != e->dim || e->wcls.rows != e->vocab || e->wcls.n != e->dim)
     return fail(B200FWD_EINVAL, "the embedding or classifier does not match the plan's sizes");
   CHECK(upload_floats(e, ck, size, dev, p.rms_att_weight, "rms_att_weight", (int64_t)e->layers * e->dim, &e->attW));
@@ -641,7 +719,8 @@ int b200fwd_generate_greedy(b200fwd_engine *e, int32_t n, const int32_t *slots, 
     }
     m[4 * T] = 0;
     m[4 * T + 1] = 0;
-    B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T + 2) * 4, cudaMemcpyHostToDevice, e->stream));
+    m[4 * T + 2] = 0;
+    B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T + 3) * 4, cudaMemcpyHostToDevice, e->stream));
     // one step, captured once and replayed: the forward pass of every slot's token, the argmax, and the step's
     // bookkeeping (the argmax becomes the next token, the positions move on), with no host in between
     cudaGraph_t graph = nullptr;
@@ -673,6 +752,7 @@ int b200fwd_generate_greedy(b200fwd_engine *e, int32_t n, const int32_t *slots, 
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphLaunch");
     if (se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
     B200_CUDA(cudaMemcpy(out, e->history, (size_t)n * steps * 4, cudaMemcpyDeviceToHost));
+    CHECK(check_tc(e));
     int32_t bad = 0;
     B200_CUDA(cudaMemcpy(&bad, e->bad_d(), 4, cudaMemcpyDeviceToHost));
     if (bad)

@@ -1,0 +1,390 @@
+// gemm_tc.cu — the int8 group-32 matmul of a prompt block or of many sequences' tokens on the 5th-generation tensor
+// cores: kernel_relaxed.ts:34-67 / 164-183 (matmul_q8r, matmul_q8r_tile) for count >= 16 tokens, to the bit.
+//
+// The reference's number for (row r, token t) is a float chain over the row's groups of 32: each group's exact
+// integer dot(w, q - 64) times (weight scale x activation scale), rounded once, added into lane g % 4 for the groups
+// below the last four, the lanes added ((0 + 1) + 2) + 3, then the groups past the fours one at a time. Here:
+//   - TMA brings 128 weight rows x 128 bytes (four groups) and BN tokens' activations x 128 bytes per stage into
+//     shared memory (128-byte swizzle; no multicast);
+//   - one thread issues one tcgen05.mma kind::i8 per group (K = 32: exactly one group) into a TMEM slot of its own
+//     (128 lanes = rows, BN columns = tokens): every group's int32 sums, exact, none added to another;
+//   - 16 epilogue warps, four per TMEM lane quarter, one per chain lane k = g % 4, read their groups' sums
+//     (tcgen05.ld) and run the reference's chain for every token of their rows with paired float32 operations
+//     (add/mul .rn .f32x2: each element rounded on its own, as f32x4 in WASM); then the four lanes meet in shared
+//     memory, are added in order, and the lane-0 warps add the groups past the fours.
+// Every mbarrier wait has an iteration limit: past it the kernel records an error and returns (no hang).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <string>
+
+#include "common.h"
+#include "gemm_tc.h"
+
+namespace b200 {
+namespace {
+
+constexpr int BM = 128;                 // rows of a tile (TMEM lanes)
+constexpr int KSTAGE = 128;             // bytes of K per stage: four groups
+constexpr int STAGES = 4;
+constexpr int EPI_WARPS = 16;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// true when the phase of `parity` completed; false when the wait gave up, or another warp of the grid already did
+// (the error flag is then set and every later wait returns at once: the kernel runs to its end and frees TMEM)
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *error, int code) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+    if (*(volatile int *)error) return false;
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicCAS(error, 0, code);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart
+__device__ __forceinline__ uint64_t smem_desc(const void *p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3fff;            // start address
+  d |= (uint64_t)1 << 16;               // leading byte offset (unused for swizzled K-major): 16 bytes
+  d |= (uint64_t)(1024 >> 4) << 32;     // stride byte offset: 8 rows of 128 bytes
+  d |= (uint64_t)1 << 46;               // version (Blackwell)
+  d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+  return d;
+}
+
+// instruction descriptor: kind::i8, D int32, A and B signed int8, both K-major, M = 128, N = bn
+__host__ __device__ constexpr uint32_t idesc_i8(int bn) {
+  return (2u << 4)                         // D format: S32
+         | (1u << 7) | (1u << 10)          // A, B: signed 8-bit
+         | ((uint32_t)(bn >> 3) << 17)     // N >> 3
+         | ((uint32_t)(BM >> 4) << 24);    // M >> 4
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// two float32 lanes at once, each rounded on its own (PTX add/mul .rn .f32x2)
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// an int32 below 2^22 in magnitude as float32, exactly: its bits added to those of 1.5 * 2^23, less 1.5 * 2^23
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;
+constexpr float MAGIC = 12582912.0f;
+
+struct Smem {
+  alignas(1024) uint8_t a[STAGES][BM * KSTAGE];
+  // b and comb are sized for the largest BN (64)
+  alignas(1024) uint8_t b[STAGES][64 * KSTAGE];
+  float comb[3][64][BM];        // the chain lanes 1..3 of every (token, row), for lane 0's warp
+  float xs[4][2][64];           // a group's activation scales, per chain lane, double-buffered
+  uint64_t full[STAGES], empty[STAGES];
+  uint64_t slot_full[32], slot_empty[32];
+  uint32_t tmem_base;
+};
+
+template <int BN>
+__global__ void __maxnreg__(112)
+    q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
+  extern __shared__ uint8_t raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  constexpr int SLOTS = 512 / BN;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng = args.n >> 5, ng4 = ng & ~3;
+  const int kstages = (args.n + KSTAGE - 1) / KSTAGE;
+  const int row0 = blockIdx.y * BM, tok0 = blockIdx.x * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; i++) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < SLOTS; i++) {
+      mbar_init(&s.slot_full[i], 1);
+      mbar_init(&s.slot_empty[i], 4);  // the four lane quarters' warps that read the slot
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // TMEM: 512 columns, the whole of this SM's (one block per SM)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&s.tmem_base)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    // ---- producer: the weight and activation tiles of every stage
+    if (lane == 0) {
+      const int wy = args.w_row0 + row0;
+      for (int k = 0; k < kstages; k++) {
+        const int st = k % STAGES;
+        if (!mbar_wait(&s.empty[st], ((k / STAGES) & 1) ^ 1, args.error, 1)) break;
+        mbar_expect_tx(&s.full[st], BM * KSTAGE + BN * KSTAGE);
+        tma_load_2d(s.a[st], &wmap, &s.full[st], k * KSTAGE, wy);
+        tma_load_2d(s.b[st], &xmap, &s.full[st], k * KSTAGE, tok0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue: one MMA per group into its slot
+    const uint32_t idesc = idesc_i8(BN);
+    for (int k = 0; k < kstages; k++) {
+      const int st = k % STAGES;
+      if (!mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 2)) break;
+      tc_fence_after();
+      bool ok = true;
+      for (int j = 0; j < 4; j++) {
+        const int g = k * 4 + j;
+        if (g >= ng) break;
+        const int slot = g % SLOTS;
+        if (!mbar_wait(&s.slot_empty[slot], ((g / SLOTS) & 1) ^ 1, args.error, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          mma_i8(tmem + (uint32_t)(slot * BN), smem_desc(s.a[st] + 32 * j), smem_desc(s.b[st] + 32 * j), idesc);
+          mma_commit(&s.slot_full[slot]);
+        }
+        __syncwarp();
+      }
+      if (lane == 0) mma_commit(&s.empty[st]);
+      __syncwarp();
+      if (!ok) break;
+    }
+  } else {
+    // ---- epilogue: warp w = 2 + 4c + q reads lane quarter q (TMEM lanes 32q..32q+31) for chain lane c
+    const int e = warp - 2, quarter = warp % 4, chain = e / 4;
+    const int r = row0 + quarter * 32 + lane;        // this thread's row
+    const int rr = r < args.rows ? r : args.rows - 1;  // (rows past the matrix read the last one, store nothing)
+    const float *ws = args.ws + (int64_t)(args.w_row0 + rr) * ng;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    uint64_t acc[BN / 2];
+#pragma unroll
+    for (int i = 0; i < BN / 2; i++) acc[i] = 0;
+    int iter = 0;
+    // one group: its sums times the scales, added into acc (every call passes the chain lane's named barrier, so
+    // the four warps of the lane stay in step even after an error)
+    auto group = [&](int g, uint64_t *accp) {
+      // this group's activation scales, shared by the four warps of the chain lane
+      float *xsb = s.xs[chain][iter & 1];
+      if (lane < BN / 4) {
+        const int t = tok0 + quarter * (BN / 4) + lane;
+        xsb[quarter * (BN / 4) + lane] = t < args.count ? args.xs[(int64_t)t * args.s_stride + g] : 0.0f;
+      }
+      named_sync(1 + chain, 128);
+      iter++;
+      const int slot = g % SLOTS;
+      mbar_wait(&s.slot_full[slot], (g / SLOTS) & 1, args.error, 4);
+      tc_fence_after();
+      const float w = __ldg(ws + g);
+      const uint64_t ww = pack2(w, w), magic = pack2(-MAGIC, -MAGIC);
+#pragma unroll
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_addr + (uint32_t)(slot * BN + c), v);
+        tmem_wait_ld();
+        if (c + 16 >= BN) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 x4 = *reinterpret_cast<const float4 *>(xsb + c + i);
+          const uint64_t f01 = add2(pack2(__uint_as_float(v[i] + MAGIC_BITS), __uint_as_float(v[i + 1] + MAGIC_BITS)), magic);
+          const uint64_t f23 = add2(pack2(__uint_as_float(v[i + 2] + MAGIC_BITS), __uint_as_float(v[i + 3] + MAGIC_BITS)), magic);
+          const uint64_t s01 = mul2(ww, pack2(x4.x, x4.y)), s23 = mul2(ww, pack2(x4.z, x4.w));
+          accp[(c + i) / 2] = add2(accp[(c + i) / 2], mul2(f01, s01));
+          accp[(c + i) / 2 + 1] = add2(accp[(c + i) / 2 + 1], mul2(f23, s23));
+        }
+      }
+    };
+    for (int g = chain; g < ng4; g += 4) group(g, acc);
+    // the chain lanes meet: 1..3 hand theirs to lane 0's warp of the same quarter
+    if (chain > 0) {
+#pragma unroll
+      for (int i = 0; i < BN / 2; i++) {
+        s.comb[chain - 1][2 * i][quarter * 32 + lane] = lo(acc[i]);
+        s.comb[chain - 1][2 * i + 1][quarter * 32 + lane] = hi(acc[i]);
+      }
+    }
+    named_sync(5 + quarter, 128);
+    if (chain == 0) {
+      // ((lane 0 + lane 1) + lane 2) + lane 3
+#pragma unroll
+      for (int i = 0; i < BN / 2; i++) {
+        uint64_t v = acc[i];
+        for (int c = 0; c < 3; c++)
+          v = add2(v, pack2(s.comb[c][2 * i][quarter * 32 + lane], s.comb[c][2 * i + 1][quarter * 32 + lane]));
+        acc[i] = v;
+      }
+      // the groups past the fours, one at a time
+      for (int g = ng4; g < ng; g++) group(g, acc);
+      if (r < args.rows) {
+        float *out = args.out + r;
+#pragma unroll
+        for (int i = 0; i < BN / 2; i++) {
+          const int t = tok0 + 2 * i;
+          if (t < args.count) {
+            float *o = out + (int64_t)t * args.out_stride;
+            *o = args.accumulate ? __fadd_rn(*o, lo(acc[i])) : lo(acc[i]);
+          }
+          if (t + 1 < args.count) {
+            float *o = out + (int64_t)(t + 1) * args.out_stride;
+            *o = args.accumulate ? __fadd_rn(*o, hi(acc[i])) : hi(acc[i]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t row_bytes, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200FWD_ECUDA, "cuTensorMapEncodeTiled is not available");
+  if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16)
+    return fail(B200FWD_EINVAL, "a TMA tensor must start on, and have rows of, multiples of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)KSTAGE, (cuuint32_t)box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200FWD_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return 0;
+}
+
+size_t gemm_smem_bytes() { return sizeof(Smem) + 1024; }
+
+int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmArgs &args, int bn,
+                   cudaStream_t stream) {
+  if (args.count <= 0 || args.rows <= 0) return 0;
+  if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
+  if (bn != 16 && bn != 32 && bn != 64) return fail(B200FWD_EINVAL, "gemm: BN must be 16, 32 or 64");
+  const size_t smem = gemm_smem_bytes();
+  dim3 grid((args.count + bn - 1) / bn, (args.rows + BM - 1) / BM);
+  static std::atomic<uint64_t> opted{0};
+  int device = 0;
+  B200_CUDA(cudaGetDevice(&device));
+  const uint64_t bit = device < 64 ? (1ull << device) : 0;
+  if (!bit || !(opted.load() & bit)) {
+    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (bit) opted.fetch_or(bit);
+  }
+  if (bn == 16)
+    q8_gemm_tc<16><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+  else if (bn == 32)
+    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+  else
+    q8_gemm_tc<64><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+  B200_LAUNCHED("q8_gemm_tc");
+  return 0;
+}
+
+int prepare_gemm() {
+  const size_t smem = gemm_smem_bytes();
+  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  return 0;
+}
+
+}  // namespace b200

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(MV_WARPS * 32)
           const uint4 wb = __ldg(reinterpret_cast<const uint4 *>(wrow + (int64_t)g * 32 + 16));
           const float sw = __ldg(srow + g);
           int corr = 0;
-          if (RELAXED) {
+          if (RELAXED && !jobs.signed_input) {
             if (crow) {
               corr = __ldg(crow + g);
             } else {
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(MV_WARPS * 32)
 
 // one group of 32 values (a lane each) quantized as kernel.ts:129-156: groupMax's lane-class maxima, then the
 // scalar comparisons; the scale, its inverse, and each value's rounding
-__device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8_t *xq, float *xs) {
+__device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8_t *xq, float *xs, int shift) {
   float m = fabsf(v);
   m = wmax(m, __shfl_xor_sync(FULL, m, 4));
   m = wmax(m, __shfl_xor_sync(FULL, m, 8));
@@ -169,7 +169,7 @@ __device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8
   if (m3 > amax) amax = m3;
   const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
   const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
-  xq[lane] = quantize_one(v, inv, bias);
+  xq[lane] = (int8_t)(quantize_one(v, inv, bias) - shift);
   if (lane == 0) *xs = scale;
 }
 
@@ -197,7 +197,7 @@ __device__ __forceinline__ float norm_scale(const float *x, int n, float eps, fl
 __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias,
                                      int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride,
                                      const int32_t *channels, int nch, float *picked, float *out_f,
-                                     int64_t out_stride) {
+                                     int64_t out_stride, int shift) {
   __shared__ float part[5];
   const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   const float *xr = x + (int64_t)tok * x_stride;
@@ -213,7 +213,7 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
         v = 0.0f;
       }
     }
-    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
   }
 }
 
@@ -236,19 +236,19 @@ __global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh
 }
 
 __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq,
-                                int64_t q_stride, float *xs, int64_t s_stride) {
+                                int64_t q_stride, float *xs, int64_t s_stride, int shift) {
   const int lane = threadIdx.x & 31;
   const int ng = n >> 5;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= (int64_t)ng * count) return;
   const int tok = (int)(gw / ng), g = (int)(gw % ng);
   const float v = x[(int64_t)tok * x_stride + g * 32 + lane];
-  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
 }
 
 // kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x
 __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int count,
-                                       int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride) {
+                                       int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int shift) {
   const int lane = threadIdx.x & 31;
   const int ng = n >> 5, n4 = n & ~3;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -258,7 +258,7 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
   const float v = h1[(int64_t)tok * stride + j];
   const float e = j < n4 ? vexp(-v) : fexp(-v);
   const float o = fmul(fdiv(v, fadd(1.0f, e)), h3[(int64_t)tok * stride + j]);
-  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g);
+  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
 }
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim,
@@ -619,32 +619,33 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
 
 int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
                          int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
-                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream) {
+                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
   norm_quantize_kernel<<<count, 256, 0, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, channels,
-                                                  nch, picked, out_f, out_stride);
+                                                  nch, picked, out_f, out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;
 }
 
 int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
-                    float *xs, int64_t s_stride, cudaStream_t stream) {
+                    float *xs, int64_t s_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "quantize_x: n must be whole groups of 32");
   const int64_t warps = (int64_t)(n / 32) * count;
-  quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride);
+  quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride,
+                                                            shift);
   B200_LAUNCHED("quantize_kernel");
   return 0;
 }
 
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
-                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream) {
+                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
   const int64_t warps = (int64_t)(n / 32) * count;
   swiglu_quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq, q_stride, xs,
-                                                                   s_stride);
+                                                                   s_stride, shift);
   B200_LAUNCHED("swiglu_quantize_kernel");
   return 0;
 }

@@ -25,24 +25,27 @@ struct MatJobs {
   int njobs;
   int n;
   int total_rows;
+  int signed_input;   // the activations are already less the bias (q - 64): a group's integer is dot(w, x)
 };
 
 // kernel_relaxed.ts:34-67/164-183 (relaxed) or kernel.ts:231-251 (8-bit): count tokens of activations
 int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_t q_stride, int64_t s_stride,
                   int count, bool relaxed, cudaStream_t stream);
 
+// The quantizing kernels below store each int8 less `shift` (0: the reference's bytes; 64 with bias 64: q - 64,
+// the signed values whose dot products with the weights are the reference's corrected group integers).
 // kernel.ts:330-342 rmsnorm then kernel.ts:129-156 quantize_x of its output, per token; channels (nch of them,
 // device) are taken out of the normalized vector first (forward.js:525-528: picked[c] = value, value = 0).
 // out_f (nullable) also gets the normalized floats.
 int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
                          int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
-                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream);
+                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift = 0);
 // kernel.ts:129-156 quantize_x, per token
 int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
-                    float *xs, int64_t s_stride, cudaStream_t stream);
+                    float *xs, int64_t s_stride, cudaStream_t stream, int shift = 0);
 // kernel.ts:654-667 swiglu then quantize_x of its output, per token
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
-                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream);
+                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream, int shift = 0);
 // forward.js:403-414 embed of int8 rows: x[t][i] = w[token*dim+i] * s[(token*dim+i)/group]; tokens on the device
 int launch_embed(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim, float *x,
                  int64_t x_stride, cudaStream_t stream);

@@ -111,6 +111,55 @@ def test_matmul_q8r_large_random(lib):
                 assert np.array_equal(bits(got[t]), bits(want)), (n, count, t)
 
 
+def matmul_signed(lib, xq7, xs, w, ws, n, count):
+    """b200k_matmul_q8s: activations of quantize_x(bias 64) handed over less the bias."""
+    rows = w.size // n
+    qs = ((n + 15) // 16) * 16
+    xsg = np.zeros((count, qs), np.int8)
+    xsg[:, :n] = (xq7[:count].astype(np.int16) - 64).astype(np.int8)
+    dq, ds, dw, dws = dev(xsg), dev(np.ascontiguousarray(xs[:count], np.float32)), dev(w), dev(ws)
+    out = full((count, rows), -7.0)
+    abi.check(lib.b200k_matmul_q8s(ptr(out), ptr(dq), ptr(ds), ptr(dw), ptr(dws), n, rows, count, rows, qs,
+                                   xs.shape[1], None))
+    return host(out)
+
+
+@pytest.mark.parametrize("n,rows", [(4096, 6144), (14336, 300), (288, 768), (160, 64), (4096, 1024)])
+def test_matmul_tensor_cores(lib, n, rows):
+    """The tensor-core path (count >= 16 tokens) to the bit against the oracle's matmul_q8r, at the 8B and stories
+    shapes and at widths with groups past the fours (288: 9 groups; 160: 5), every token tile width."""
+    rng = np.random.default_rng(n + rows)
+    w = rng.integers(-128, 128, size=rows * n, dtype=np.int8)
+    w[:32] = -128
+    ws = rng.uniform(0.001, 0.02, rows * n // 32).astype(np.float32)
+    wc = oracle.int8_sums(w)
+    count_max = 200
+    x = rng.standard_normal((count_max, n)).astype(np.float32) * rng.uniform(0.1, 10, (count_max, 1)).astype(np.float32)
+    xq = np.zeros((count_max, n), np.int8)
+    xs = np.zeros((count_max, n // 32), np.float32)
+    for t in range(count_max):
+        xq[t], xs[t] = oracle.quantize_x(x[t], 64)
+    xq[0, :] = 127
+    want = np.stack([oracle.matmul_q8r(xq[t], xs[t], w, ws, wc, n) for t in range(count_max)])
+    for count in (16, 17, 64, 100, 200):
+        got = matmul_signed(lib, xq, xs, w, ws, n, count)
+        assert np.array_equal(bits(got), bits(want[:count])), count
+
+
+def test_matmul_tensor_cores_formula(lib, mm):
+    """forward-check.mjs's matmul_q8r formula through the tensor-core path: its activations repeated to 24 tokens."""
+    for groups in mm.GROUPS:
+        m = groups * 32
+        w = mm.q8r_weights(groups)
+        ws = mm.ws[:mm.rows * groups]
+        want = mm.q8r_expected(w, groups)
+        xq = np.tile(mm.x7[:m], (24, 1))
+        xs = np.tile(mm.xs[:groups], (24, 1))
+        got = matmul_signed(lib, xq, xs, w, ws, m, 24)
+        for t in range(24):
+            assert np.array_equal(bits(got[t]), bits(want)), (groups, t)
+
+
 def test_quantize_x(lib):
     rng = np.random.default_rng(4)
     n, count = 4096 + 96, 5

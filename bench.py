@@ -179,11 +179,12 @@ def reference_arm(args):
 
 
 def matmul_roofline(lib, M, stream, peaks, reps=12):
-    """The int8 matmul alone at the decode step's shapes: every matrix of a layer (q, k, v, o, w1, w3, w2) at M
-    tokens, cycling over 8 distinct layers' worth of weights (2 GB, beyond L2). CUDA events on the stream."""
+    """The int8 matmul alone at the decode step's shapes, as the engine runs them (q|k|v fused, o, w1|w3 fused, w2)
+    at M tokens through b200k_matmul_q8s (the tensor cores from 16 tokens on), cycling over 8 distinct layers'
+    worth of weights (2 GB, beyond L2). CUDA events on the stream."""
     import torch
 
-    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
     layers = 8
     g = torch.Generator(device="cuda")
     g.manual_seed(1)
@@ -193,18 +194,18 @@ def matmul_roofline(lib, M, stream, peaks, reps=12):
         s = torch.rand((layers, rows, n // 32), device="cuda", generator=g) * 0.019 + 0.001
         mats.append((w, s, rows, n))
     nmax = 14336
-    xq = torch.randint(1, 128, (M, nmax), dtype=torch.int8, device="cuda", generator=g)
+    xq = torch.randint(-63, 64, (M, nmax), dtype=torch.int8, device="cuda", generator=g)
     xs = torch.rand((M, nmax // 32), device="cuda", generator=g) * 0.1
-    out = torch.empty((M, 14336), device="cuda")
+    out = torch.empty((M, 28672), device="cuda")
     st = torch.cuda.ExternalStream(stream)
     import ctypes
 
     def launch(i):
         w, s, rows, n = mats[i % len(mats)]
         layer = (i // len(mats)) % layers
-        rc = lib.b200k_matmul_q8r(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(xq.data_ptr()),
+        rc = lib.b200k_matmul_q8s(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(xq.data_ptr()),
                                   ctypes.c_void_p(xs.data_ptr()), ctypes.c_void_p(w[layer].data_ptr()),
-                                  ctypes.c_void_p(s[layer].data_ptr()), None, n, 0, rows, M, 14336, nmax, nmax // 32,
+                                  ctypes.c_void_p(s[layer].data_ptr()), n, rows, M, 28672, nmax, nmax // 32,
                                   ctypes.c_void_p(stream))
         assert rc == 0
         return rows * n * (1 + 4 / 32) + M * n * (1 + 4 / 32) + M * rows * 4
@@ -227,7 +228,8 @@ def matmul_roofline(lib, M, stream, peaks, reps=12):
     peak = float(peaks["hbm_gbs"])
     del mats
     torch.cuda.empty_cache()
-    return {"kernel": "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
+    return {"kernel": "q8_gemm_tc (int8 group-32 matmul, tcgen05, exact order)" if M >= 16 else
+            "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": None, "M": M, "per_launch_us": per_launch_s * 1e6,
             "algorithmic_bytes_per_launch": per_launch_bytes}

@@ -89,7 +89,7 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     int *err = nullptr;
     B200_CUDA(cudaGetSymbolAddress((void **)&err, capi_tc_error));
     const int row_tiles = (rows + 127) / 128;
-    int bn = 64;
+    int bn = 32;
     while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
     CUtensorMap wmap, xmap;
     int rc = make_i8_map(&wmap, wq, n, rows, n, 128);

@@ -95,7 +95,7 @@ struct b200fwd_engine {
   int logit_rows = 0;
   int32_t *argmax = nullptr;
   int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tensor-core error
-  CUtensorMap xmap[3];          // the activations for the tensor cores' tiles of 16, 32 and 64 tokens
+  CUtensorMap xmap[2];          // the activations for the tensor cores' tiles of 16 and 32 tokens
   bool tensor_cores = true;
   int32_t *meta_h = nullptr;    // pinned host copy
   int32_t *history = nullptr;   // greedy ids [slots][steps]
@@ -241,11 +241,11 @@ int alloc_activations(b200fwd_engine *e) {
   CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 4) * 4));
   B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 4) * 4, e->stream));
   B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 4) * 4));
-  // the activations' TMA maps (rows of XQ bytes, one per token), for tiles of 16, 32 and 64 tokens
-  const int bns[3] = {16, 32, 64};
-  e->tensor_cores = e->tensor_cores && T >= 64 && e->XQ >= 128;
+  // the activations' TMA maps (rows of XQ bytes, one per token), for tiles of 16 and 32 tokens
+  const int bns[2] = {16, 32};
+  e->tensor_cores = e->tensor_cores && T >= 32 && e->XQ >= 128;
   if (e->tensor_cores)
-    for (int i = 0; i < 3; i++) CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
+    for (int i = 0; i < 2; i++) CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
   return 0;
 }
 
@@ -303,9 +303,9 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
     a.accumulate = accumulate;
     // the widest token tile that still gives every SM a tile
     const int row_tiles = (m.rows + 127) / 128;
-    int bn = 64;
+    int bn = 32;
     while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
-    const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
+    const int which = bn == 16 ? 0 : 1;
     return launch_gemm_tc(m.map, e->xmap[which], a, bn, e->stream);
   }
   MatJobs jobs{};

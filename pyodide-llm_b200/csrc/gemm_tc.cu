@@ -28,7 +28,8 @@ namespace {
 
 constexpr int BM = 128;                 // rows of a tile (TMEM lanes)
 constexpr int KSTAGE = 128;             // bytes of K per stage: four groups
-constexpr int STAGES = 4;
+constexpr int STAGES = 6;
+constexpr int BN_MAX = 32;            // tokens of a tile at most (32 accumulators a thread)
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
@@ -147,17 +148,17 @@ constexpr float MAGIC = 12582912.0f;
 
 struct Smem {
   alignas(1024) uint8_t a[STAGES][BM * KSTAGE];
-  // b and comb are sized for the largest BN (64)
-  alignas(1024) uint8_t b[STAGES][64 * KSTAGE];
-  float comb[3][64][BM];        // the chain lanes 1..3 of every (token, row), for lane 0's warp
-  float xs[4][2][64];           // a group's activation scales, per chain lane, double-buffered
+  // b and comb are sized for the largest BN
+  alignas(1024) uint8_t b[STAGES][BN_MAX * KSTAGE];
+  float comb[3][BN_MAX][BM];    // the chain lanes 1..3 of every (token, row), for lane 0's warp
+  float xs[4][2][BN_MAX];       // a group's activation scales, per chain lane, double-buffered
   uint64_t full[STAGES], empty[STAGES];
   uint64_t slot_full[32], slot_empty[32];
   uint32_t tmem_base;
 };
 
 template <int BN>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
   extern __shared__ uint8_t raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -252,7 +253,6 @@ __global__ void __maxnreg__(112)
       mbar_wait(&s.slot_full[slot], (g / SLOTS) & 1, args.error, 4);
       tc_fence_after();
       const float w = __ldg(ws + g);
-      const uint64_t ww = pack2(w, w), magic = pack2(-MAGIC, -MAGIC);
 #pragma unroll
       for (int c = 0; c < BN; c += 16) {
         uint32_t v[16];
@@ -266,11 +266,15 @@ __global__ void __maxnreg__(112)
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
           const float4 x4 = *reinterpret_cast<const float4 *>(xsb + c + i);
-          const uint64_t f01 = add2(pack2(__uint_as_float(v[i] + MAGIC_BITS), __uint_as_float(v[i + 1] + MAGIC_BITS)), magic);
-          const uint64_t f23 = add2(pack2(__uint_as_float(v[i + 2] + MAGIC_BITS), __uint_as_float(v[i + 3] + MAGIC_BITS)), magic);
-          const uint64_t s01 = mul2(ww, pack2(x4.x, x4.y)), s23 = mul2(ww, pack2(x4.z, x4.w));
-          accp[(c + i) / 2] = add2(accp[(c + i) / 2], mul2(f01, s01));
-          accp[(c + i) / 2 + 1] = add2(accp[(c + i) / 2 + 1], mul2(f23, s23));
+          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+          for (int j = 0; j < 4; j += 2) {
+            const uint64_t a = accp[(c + i + j) / 2];
+            const float f0 = __fsub_rn(__uint_as_float(v[i + j] + MAGIC_BITS), MAGIC);
+            const float f1 = __fsub_rn(__uint_as_float(v[i + j + 1] + MAGIC_BITS), MAGIC);
+            const float p0 = __fmul_rn(f0, __fmul_rn(w, xv[j])), p1 = __fmul_rn(f1, __fmul_rn(w, xv[j + 1]));
+            accp[(c + i + j) / 2] = pack2(__fadd_rn(lo(a), p0), __fadd_rn(hi(a), p1));
+          }
         }
       }
     };
@@ -320,6 +324,12 @@ __global__ void __maxnreg__(112)
   }
 }
 
+#define CHECK_RC(expr)   \
+  do {                   \
+    int rc_ = (expr);    \
+    if (rc_) return rc_; \
+  } while (0)
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -356,7 +366,7 @@ int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmA
                    cudaStream_t stream) {
   if (args.count <= 0 || args.rows <= 0) return 0;
   if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
-  if (bn != 16 && bn != 32 && bn != 64) return fail(B200FWD_EINVAL, "gemm: BN must be 16, 32 or 64");
+  if (bn != 16 && bn != 32) return fail(B200FWD_EINVAL, "gemm: BN must be 16 or 32");
   const size_t smem = gemm_smem_bytes();
   dim3 grid((args.count + bn - 1) / bn, (args.rows + BM - 1) / BM);
   static std::atomic<uint64_t> opted{0};
@@ -364,17 +374,13 @@ int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmA
   B200_CUDA(cudaGetDevice(&device));
   const uint64_t bit = device < 64 ? (1ull << device) : 0;
   if (!bit || !(opted.load() & bit)) {
-    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    CHECK_RC(prepare_gemm());
     if (bit) opted.fetch_or(bit);
   }
   if (bn == 16)
     q8_gemm_tc<16><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
-  else if (bn == 32)
-    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
   else
-    q8_gemm_tc<64><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
   B200_LAUNCHED("q8_gemm_tc");
   return 0;
 }
@@ -383,7 +389,6 @@ int prepare_gemm() {
   const size_t smem = gemm_smem_bytes();
   B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   return 0;
 }
 

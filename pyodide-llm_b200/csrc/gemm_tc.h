@@ -21,7 +21,7 @@ struct GemmArgs {
 // a 2-D TMA map over int8 rows: cols bytes of rows rows, row_bytes apart; boxes of 128 bytes x box_rows rows,
 // 128-byte swizzle (the layout the tcgen05 descriptors of gemm_tc.cu read)
 int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t row_bytes, int box_rows);
-// wmap: the weights (box rows 128); xmap: the activations, already less the bias of 64 (box rows bn)
+// wmap: the weights (box rows 128); xmap: the activations, already less the bias of 64 (box rows bn: 16 or 32)
 int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmArgs &args, int bn,
                    cudaStream_t stream);
 // the kernels' shared-memory opt-in on the current device (before any graph capture)

@@ -205,8 +205,8 @@ def matmul_roofline(lib, M, stream, peaks, reps=12):
         layer = (i // len(mats)) % layers
         rc = lib.b200k_matmul_q8s(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(xq.data_ptr()),
                                   ctypes.c_void_p(xs.data_ptr()), ctypes.c_void_p(w[layer].data_ptr()),
-                                  ctypes.c_void_p(s[layer].data_ptr()), n, rows, M, 28672, nmax, nmax // 32,
-                                  ctypes.c_void_p(stream))
+                                  ctypes.c_void_p(s[layer].data_ptr()), n // 32, n, rows, M, 28672, nmax,
+                                  nmax // 32, ctypes.c_void_p(stream))
         assert rc == 0
         return rows * n * (1 + 4 / 32) + M * n * (1 + 4 / 32) + M * rows * 4
 

@@ -169,11 +169,12 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream);
 /* kernel_relaxed.ts:34-67 / 164-183 on activations already less the bias (xq[i] = q[i] - 64, signed; the engine
  * keeps them so): all `rows` rows of W for `count` tokens, the same numbers to the bit. From 16 tokens on (with
- * n >= 128 and rows >= 128) it runs on the tensor cores (tcgen05.mma kind::i8, one MMA per group of 32), below on
- * the CUDA cores. xq and wq 16-byte aligned, q_stride a multiple of 16. */
-int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
-                     int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
-                     b200fwd_stream stream);
+ * n >= 128, rows >= 128, and ws_stride, s_stride multiples of 4 floats: TMA rows of whole 16 bytes) it runs on the
+ * tensor cores (tcgen05.mma kind::i8, one MMA per group of 32), else on the CUDA cores. ws: row r's scales at
+ * ws + r * ws_stride (0: n / 32). xq, wq, ws, xs 16-byte aligned; q_stride a multiple of 16. */
+int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                     int64_t ws_stride, int32_t n, int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride,
+                     int64_t s_stride, b200fwd_stream stream);
 /* kernel.ts:231-258 matmul_q8: the same on quantize_x(bias 0) activations, lane order of dot32. */
 int b200k_matmul_q8(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
                     int32_t r0, int32_t r1, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,

@@ -144,7 +144,7 @@ def load():
         "b200k_int8_sums": (P, P, I64, P),
         "b200k_matmul_q8r": (P, P, P, P, P, P, I32, I32, I32, I32, I64, I64, I64, P),
         "b200k_matmul_q8": (P, P, P, P, P, I32, I32, I32, I32, I64, I64, I64, P),
-        "b200k_matmul_q8s": (P, P, P, P, P, I32, I32, I32, I64, I64, I64, P),
+        "b200k_matmul_q8s": (P, P, P, P, P, I64, I32, I32, I32, I64, I64, I64, P),
         "b200k_rmsnorm": (P, P, P, I32, ctypes.c_float, I32, I64, P),
         "b200k_rope": (P, P, P, I32, I32, I32, P),
         "b200k_attention": (P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, P),

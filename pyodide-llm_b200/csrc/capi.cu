@@ -67,19 +67,23 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
   });
 }
 
-int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
-                     int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,
-                     b200fwd_stream stream) {
+int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                     int64_t ws_stride, int32_t n, int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride,
+                     int64_t s_stride, b200fwd_stream stream) {
   return guarded([&] {
     if (!xout || !xq || !xs || !wq || !ws) return fail(B200FWD_EINVAL, "matmul_q8s: null pointer");
     if (n <= 0 || n % 32 || rows < 0 || count < 0) return fail(B200FWD_EINVAL, "matmul_q8s: bad sizes");
     if (rows == 0 || count == 0) return 0;
     if (q_stride % 16 || (reinterpret_cast<uintptr_t>(xq) % 16) || (reinterpret_cast<uintptr_t>(wq) % 16))
       return fail(B200FWD_EINVAL, "matmul_q8s: weights and activations must be 16-byte aligned");
+    if (ws_stride == 0) ws_stride = n / 32;
+    if (ws_stride < n / 32) return fail(B200FWD_EINVAL, "matmul_q8s: ws_stride below n / 32");
     cudaStream_t st = as_stream(stream);
-    if (count < 16 || n < 128 || rows < 128) {
+    // the tensor cores need whole TMA boxes and scale rows of whole 16 bytes: else the CUDA cores
+    if (count < 16 || n < 128 || rows < 128 || ws_stride % 4 || s_stride % 4 ||
+        (reinterpret_cast<uintptr_t>(ws) % 16) || (reinterpret_cast<uintptr_t>(xs) % 16)) {
       MatJobs jobs{};
-      jobs.job[0] = {wq, ws, nullptr, xout, rows, 0, out_stride};
+      jobs.job[0] = {wq, ws, nullptr, xout, rows, 0, out_stride, (int)ws_stride};
       jobs.njobs = 1;
       jobs.n = n;
       jobs.total_rows = rows;
@@ -91,23 +95,22 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     const int row_tiles = (rows + 127) / 128;
     int bn = 32;
     while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
-    CUtensorMap wmap, xmap;
-    int rc = make_i8_map(&wmap, wq, n, rows, n, 128);
-    if (!rc) rc = make_i8_map(&xmap, xq, n, count, q_stride, bn);
+    GemmMaps maps;
+    int rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
+    if (!rc) rc = make_i8_map(&maps.x, xq, n, count, q_stride, bn);
+    if (!rc) rc = make_scale_map(&maps.ws, ws, ws_stride, rows, ws_stride, 128);
+    if (!rc) rc = make_scale_map(&maps.xs, xs, n / 32, count, s_stride, bn);
     if (rc) return rc;
     GemmArgs a{};
-    a.ws = ws;
-    a.xs = xs;
     a.out = xout;
     a.error = err;
     a.n = n;
     a.rows = rows;
     a.count = count;
     a.w_row0 = 0;
-    a.s_stride = s_stride;
     a.out_stride = out_stride;
     a.accumulate = 0;
-    rc = launch_gemm_tc(wmap, xmap, a, bn, st);
+    rc = launch_gemm_tc(maps, a, bn, st);
     if (rc) return rc;
     int32_t e = 0;
     B200_CUDA(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, st));

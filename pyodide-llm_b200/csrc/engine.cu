@@ -42,15 +42,19 @@ int cuda_fail(cudaError_t e, const char *what) {
 
 namespace {
 
-// an int8 matrix of every layer (rows x n each), values then scales, and its TMA map over all layers' rows
+// an int8 matrix of every layer (rows x n each): values, and scales in rows of sstride floats (the row's n/32
+// groups, padded to a multiple of four so that a TMA row is whole 16 bytes); its TMA maps over all layers' rows
 struct Matrix {
   int8_t *w = nullptr;
   float *s = nullptr;
-  int rows = 0, n = 0, layers = 1;
-  CUtensorMap map;
+  int rows = 0, n = 0, layers = 1, sstride = 0;
+  bool mapped = false;
+  CUtensorMap wmap, smap;
   const int8_t *layer_w(int l) const { return w + (int64_t)l * rows * n; }
-  const float *layer_s(int l) const { return s + (int64_t)l * rows * (n / 32); }
+  const float *layer_s(int l) const { return s + (int64_t)l * rows * sstride; }
 };
+
+inline int padded_groups(int n) { return ((n / 32 + 3) / 4) * 4; }
 
 // kernel.ts:383-392 half on the host, for keysAndValues
 float half_bits_to_float(uint16_t h) {
@@ -95,7 +99,7 @@ struct b200fwd_engine {
   int logit_rows = 0;
   int32_t *argmax = nullptr;
   int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tensor-core error
-  CUtensorMap xmap[2];          // the activations for the tensor cores' tiles of 16 and 32 tokens
+  CUtensorMap xmap[2], xsmap[2]; // the activations and their scales, for tiles of 16 and 32 tokens
   bool tensor_cores = true;
   int32_t *meta_h = nullptr;    // pinned host copy
   int32_t *history = nullptr;   // greedy ids [slots][steps]
@@ -166,10 +170,14 @@ int upload_matrix(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_d
   const int64_t count = elements(t);
   if (t.offset < 0 || t.scales < 0 || (size_t)(t.offset + count) > size || (size_t)(t.scales + count / 8) > size)
     return fail(B200FWD_EINVAL, std::string("tensor ") + name + " lies outside the checkpoint");
+  m.sstride = padded_groups(m.n);
+  const int64_t rows_all = count / m.n;
   CHECK(alloc(e, (void **)&m.w, count));
-  CHECK(alloc(e, (void **)&m.s, count / 32 * 4));
+  CHECK(alloc(e, (void **)&m.s, rows_all * m.sstride * 4));
+  B200_CUDA(cudaMemsetAsync(m.s, 0, rows_all * m.sstride * 4, e->stream));
   B200_CUDA(cudaMemcpyAsync(m.w, ckpt + t.offset, count, copy_kind(on_device), e->stream));
-  B200_CUDA(cudaMemcpyAsync(m.s, ckpt + t.scales, count / 32 * 4, copy_kind(on_device), e->stream));
+  B200_CUDA(cudaMemcpy2DAsync(m.s, (size_t)m.sstride * 4, ckpt + t.scales, (size_t)(m.n / 32) * 4,
+                              (size_t)(m.n / 32) * 4, rows_all, copy_kind(on_device), e->stream));
   return 0;
 }
 
@@ -196,18 +204,22 @@ int upload_fused(b200fwd_engine *e, const uint8_t *ckpt, size_t size, bool on_de
   m.rows = rows;
   m.n = n;
   m.layers = layers;
+  m.sstride = padded_groups(n);
   const int64_t count = (int64_t)layers * rows * n;
+  const int ng = n / 32;
   CHECK(alloc(e, (void **)&m.w, count));
-  CHECK(alloc(e, (void **)&m.s, count / 32 * 4));
+  CHECK(alloc(e, (void **)&m.s, (int64_t)layers * rows * m.sstride * 4));
+  B200_CUDA(cudaMemsetAsync(m.s, 0, (int64_t)layers * rows * m.sstride * 4, e->stream));
   int at = 0;
   for (auto &pt : parts) {
     const b200fwd_tensor &t = *pt.first;
     const int r = (int)t.shape[1];
     B200_CUDA(cudaMemcpy2DAsync(m.w + (int64_t)at * n, (size_t)rows * n, ckpt + t.offset, (size_t)r * n, (size_t)r * n,
                                 layers, copy_kind(on_device), e->stream));
-    B200_CUDA(cudaMemcpy2DAsync(m.s + (int64_t)at * (n / 32), (size_t)rows * (n / 32) * 4, ckpt + t.scales,
-                                (size_t)r * (n / 32) * 4, (size_t)r * (n / 32) * 4, layers, copy_kind(on_device),
-                                e->stream));
+    for (int l = 0; l < layers; l++)
+      B200_CUDA(cudaMemcpy2DAsync(m.s + ((int64_t)l * rows + at) * m.sstride, (size_t)m.sstride * 4,
+                                  ckpt + t.scales + (int64_t)l * r * ng * 4, (size_t)ng * 4, (size_t)ng * 4, r,
+                                  copy_kind(on_device), e->stream));
     at += r;
   }
   return 0;
@@ -241,11 +253,15 @@ int alloc_activations(b200fwd_engine *e) {
   CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 4) * 4));
   B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 4) * 4, e->stream));
   B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 4) * 4));
-  // the activations' TMA maps (rows of XQ bytes, one per token), for tiles of 16 and 32 tokens
+  // the activations' TMA maps (rows of XQ bytes, one per token) and their scales' (rows of XQ/32 floats), for tiles
+  // of 16 and 32 tokens
   const int bns[2] = {16, 32};
   e->tensor_cores = e->tensor_cores && T >= 32 && e->XQ >= 128;
   if (e->tensor_cores)
-    for (int i = 0; i < 2; i++) CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
+    for (int i = 0; i < 2; i++) {
+      CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
+      CHECK(make_scale_map(&e->xsmap[i], e->xs, e->XQ / 32, T, e->XQ / 32, bns[i]));
+    }
   return 0;
 }
 
@@ -287,18 +303,15 @@ int grow(b200fwd_engine *e, int pos) {
 // cores from 16 tokens on (gemm_tc.cu), the CUDA cores below (kernels.cu); the same numbers either way
 int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t out_stride, int accumulate, int count) {
   const int XS = e->XQ / 32;
-  // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 64 tokens: never past the tensors' extents)
-  if (count >= 16 && e->relaxed && e->tensor_cores && m.n >= 128 && (int64_t)m.layers * m.rows >= 128) {
+  // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 32 tokens: never past the tensors' extents)
+  if (count >= 16 && e->relaxed && e->tensor_cores && m.mapped) {
     GemmArgs a{};
-    a.ws = m.s;
-    a.xs = e->xs;
     a.out = out;
     a.error = e->tc_error_d();
     a.n = m.n;
     a.rows = m.rows;
     a.count = count;
     a.w_row0 = layer * m.rows;
-    a.s_stride = XS;
     a.out_stride = out_stride;
     a.accumulate = accumulate;
     // the widest token tile that still gives every SM a tile
@@ -306,10 +319,11 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
     int bn = 32;
     while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
     const int which = bn == 16 ? 0 : 1;
-    return launch_gemm_tc(m.map, e->xmap[which], a, bn, e->stream);
+    GemmMaps maps{m.wmap, e->xmap[which], m.smap, e->xsmap[which]};
+    return launch_gemm_tc(maps, a, bn, e->stream);
   }
   MatJobs jobs{};
-  jobs.job[0] = {m.layer_w(layer), m.layer_s(layer), nullptr, out, m.rows, accumulate, out_stride};
+  jobs.job[0] = {m.layer_w(layer), m.layer_s(layer), nullptr, out, m.rows, accumulate, out_stride, m.sstride};
   jobs.njobs = 1;
   jobs.n = m.n;
   jobs.total_rows = m.rows;
@@ -324,7 +338,7 @@ int forward_device(b200fwd_engine *e, int n, int want, int max_count) {
   const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32, QKV = e->QKV;
   const int shift = e->bias;  // activations stored less the bias
   float *q = e->qkv, *k = e->qkv + QD, *v = e->qkv + QD + KVD;
-  CHECK(launch_embed(e->emb.w, e->emb.s, 32, e->tokens_d(), n, D, e->x, D, st));
+  CHECK(launch_embed(e->emb.w, e->emb.s, e->emb.sstride, e->tokens_d(), n, D, e->x, D, st));
   for (int l = 0; l < e->layers; l++) {
     CHECK(launch_norm_quantize(e->x, D, e->attW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
                                nullptr, 0, nullptr, nullptr, 0, st, shift));
@@ -432,7 +446,8 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
     return fail(B200FWD_EUNSUPPORTED, "the int8 kernels take rows of whole groups of 32");
   if (p.n_outliers < 0 || p.n_outliers > B200FWD_MAX_OUTLIERS) return fail(B200FWD_EINVAL, "bad outlier count");
   if (!p.freq_cis_real || !p.freq_cis_imag) return fail(B200FWD_EINVAL, "the plan has no RoPE tables");
-  e->XQ = std::max(std::max(e->dim, e->hidden), e->qDim);
+  // the activation rows: the widest input, rounded up to 128 bytes (whole TMA boxes; scale rows of whole 16 bytes)
+  e->XQ = (std::max(std::max(e->dim, e->hidden), e->qDim) + 127) / 128 * 128;
   e->QKV = e->qDim + 2 * e->kvDim;
   e->relaxed = p.relaxed != 0;
   e->bias = e->relaxed ? 64 : 0;
@@ -472,8 +487,12 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
       return fail(B200FWD_EINVAL, "a layer matrix's shape does not match the plan's sizes");
   Matrix *maps[] = {&e->wqkv, &e->wo, &e->w13, &e->w2, &e->wcls};
   for (Matrix *m : maps)
-    if (m->n >= 128 && (int64_t)m->layers * m->rows >= 128)
-      CHECK(make_i8_map(&m->map, m->w, m->n, (int64_t)m->layers * m->rows, m->n, 128));
+    if (m->n >= 128 && (int64_t)m->layers * m->rows >= 128) {
+      CHECK(make_i8_map(&m->wmap, m->w, m->n, (int64_t)m->layers * m->rows, m->n, 128));
+      CHECK(make_scale_map(&m->smap, m->s, m->sstride, (int64_t)m->layers * m->rows, m->sstride, 128));
+      m->mapped = true;
+    }
+
   if (e->emb.rows != e->vocab || e->emb.n != e->dim || e->wcls.rows != e->vocab || e->wcls.n != e->dim)
     return fail(B200FWD_EINVAL, "the embedding or classifier does not match the plan's sizes");
   CHECK(upload_floats(e, ck, size, dev, p.rms_att_weight, "rms_att_weight", (int64_t)e->layers * e->dim, &e->attW));
@@ -491,8 +510,8 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
   CHECK(alloc(e, (void **)&e->columns, (size_t)std::max(1, e->nch) * e->vocab * 4));
   if (e->nch) {
     B200_CUDA(cudaMemcpyAsync(e->channels, p.outliers, sizeof(int32_t) * e->nch, cudaMemcpyHostToDevice, e->stream));
-    CHECK(launch_outlier_columns(e->columns, e->wcls.w, e->wcls.s, 32, e->dim, e->vocab, e->channels, e->nch,
-                                 e->stream));
+    CHECK(launch_outlier_columns(e->columns, e->wcls.w, e->wcls.s, e->wcls.sstride, e->dim, e->vocab, e->channels,
+                                 e->nch, e->stream));
   }
   CHECK(alloc_activations(e));
   // forward.js:272-273: the cache from kv_start positions (or the caller's first capacity)

@@ -28,7 +28,7 @@ namespace {
 
 constexpr int BM = 128;                 // rows of a tile (TMEM lanes)
 constexpr int KSTAGE = 128;             // bytes of K per stage: four groups
-constexpr int STAGES = 6;
+constexpr int STAGES = 8;
 constexpr int BN_MAX = 32;            // tokens of a tile at most (32 accumulators a thread)
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
@@ -147,22 +147,42 @@ constexpr uint32_t MAGIC_BITS = 0x4B400000u;
 constexpr float MAGIC = 12582912.0f;
 
 struct Smem {
-  alignas(1024) uint8_t a[STAGES][BM * KSTAGE];
-  // b and comb are sized for the largest BN
-  alignas(1024) uint8_t b[STAGES][BN_MAX * KSTAGE];
-  float comb[3][BN_MAX][BM];    // the chain lanes 1..3 of every (token, row), for lane 0's warp
-  float xs[4][2][BN_MAX];       // a group's activation scales, per chain lane, double-buffered
+  alignas(1024) uint8_t a[STAGES][BM * KSTAGE];       // 128 weight rows x four groups
+  alignas(1024) uint8_t b[STAGES][BN_MAX * KSTAGE];   // the tokens x four groups
+  alignas(128) float ws[STAGES][BM][4];               // the rows' four groups' scales
+  alignas(128) float xs[STAGES][BN_MAX][4];           // the tokens' four groups' scales
   uint64_t full[STAGES], empty[STAGES];
   uint64_t slot_full[32], slot_empty[32];
   uint32_t tmem_base;
 };
 
+// TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes
+template <int TPW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[TPW]);
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+// Warp roles: 0 TMA producer, 1 MMA issue, 2..17 epilogue. Epilogue warp w reads TMEM lane quarter w % 4 (its 32
+// rows) and token columns (w - 2) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
+// its (row, token) in registers: the chains, their sum and the groups past the fours all happen in one thread.
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
-    q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, GemmArgs args) {
+    q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+               const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap, GemmArgs args) {
   extern __shared__ uint8_t raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   constexpr int SLOTS = 512 / BN;
+  constexpr int TPW = BN / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = args.n >> 5, ng4 = ng & ~3;
   const int kstages = (args.n + KSTAGE - 1) / KSTAGE;
@@ -171,11 +191,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
+      mbar_init(&s.empty[i], 1 + EPI_WARPS);  // the MMAs' commit, and every epilogue warp done with the scales
     }
     for (int i = 0; i < SLOTS; i++) {
       mbar_init(&s.slot_full[i], 1);
-      mbar_init(&s.slot_empty[i], 4);  // the four lane quarters' warps that read the slot
+      mbar_init(&s.slot_empty[i], EPI_WARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -189,15 +209,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = s.tmem_base;
 
   if (warp == 0) {
-    // ---- producer: the weight and activation tiles of every stage
+    // ---- producer: each stage's weights, activations and both scale tiles on one barrier
     if (lane == 0) {
       const int wy = args.w_row0 + row0;
+      constexpr uint32_t bytes = BM * KSTAGE + BN * KSTAGE + BM * 16 + BN * 16;
       for (int k = 0; k < kstages; k++) {
         const int st = k % STAGES;
         if (!mbar_wait(&s.empty[st], ((k / STAGES) & 1) ^ 1, args.error, 1)) break;
-        mbar_expect_tx(&s.full[st], BM * KSTAGE + BN * KSTAGE);
+        mbar_expect_tx(&s.full[st], bytes);
         tma_load_2d(s.a[st], &wmap, &s.full[st], k * KSTAGE, wy);
         tma_load_2d(s.b[st], &xmap, &s.full[st], k * KSTAGE, tok0);
+        tma_load_2d(s.ws[st], &wsmap, &s.full[st], k * 4, wy);
+        tma_load_2d(s.xs[st], &xsmap, &s.full[st], k * 4, tok0);
       }
     }
   } else if (warp == 1) {
@@ -228,90 +251,73 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) break;
     }
   } else {
-    // ---- epilogue: warp w = 2 + 4c + q reads lane quarter q (TMEM lanes 32q..32q+31) for chain lane c
-    const int e = warp - 2, quarter = warp % 4, chain = e / 4;
-    const int r = row0 + quarter * 32 + lane;        // this thread's row
-    const int rr = r < args.rows ? r : args.rows - 1;  // (rows past the matrix read the last one, store nothing)
-    const float *ws = args.ws + (int64_t)(args.w_row0 + rr) * ng;
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint64_t acc[BN / 2];
+    // ---- epilogue
+    const int quarter = warp % 4, sub = (warp - 2) / 4;
+    const int rl = quarter * 32 + lane;  // the row within the tile
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
+    float acc[TPW][4];
 #pragma unroll
-    for (int i = 0; i < BN / 2; i++) acc[i] = 0;
-    int iter = 0;
-    // one group: its sums times the scales, added into acc (every call passes the chain lane's named barrier, so
-    // the four warps of the lane stay in step even after an error)
-    auto group = [&](int g, uint64_t *accp) {
-      // this group's activation scales, shared by the four warps of the chain lane
-      float *xsb = s.xs[chain][iter & 1];
-      if (lane < BN / 4) {
-        const int t = tok0 + quarter * (BN / 4) + lane;
-        xsb[quarter * (BN / 4) + lane] = t < args.count ? args.xs[(int64_t)t * args.s_stride + g] : 0.0f;
-      }
-      named_sync(1 + chain, 128);
-      iter++;
-      const int slot = g % SLOTS;
-      mbar_wait(&s.slot_full[slot], (g / SLOTS) & 1, args.error, 4);
-      tc_fence_after();
-      const float w = __ldg(ws + g);
+    for (int t = 0; t < TPW; t++)
 #pragma unroll
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + lane_addr + (uint32_t)(slot * BN + c), v);
-        tmem_wait_ld();
-        if (c + 16 >= BN) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
+      for (int j = 0; j < 4; j++) acc[t][j] = 0.0f;
+    for (int k = 0; k < kstages; k++) {
+      const int st = k % STAGES;
+      mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 4);
+      const int groups = min(4, ng - 4 * k);
+      // the stage's groups' sums of this warp's tokens, then its slots go back to the MMAs
+      uint32_t v[4][TPW];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (j < groups) {
+          const int g = 4 * k + j, slot = g % SLOTS;
+          mbar_wait(&s.slot_full[slot], (g / SLOTS) & 1, args.error, 5);
+          tc_fence_after();
+          tmem_ld<TPW>(taddr + (uint32_t)(slot * BN), v[j]);
         }
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        for (int j = 0; j < groups; j++) mbar_arrive(&s.slot_empty[(4 * k + j) % SLOTS]);
+      const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 x4 = *reinterpret_cast<const float4 *>(xsb + c + i);
-          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+      for (int t = 0; t < TPW; t++) {
+        const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
+        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-          for (int j = 0; j < 4; j += 2) {
-            const uint64_t a = accp[(c + i + j) / 2];
-            const float f0 = __fsub_rn(__uint_as_float(v[i + j] + MAGIC_BITS), MAGIC);
-            const float f1 = __fsub_rn(__uint_as_float(v[i + j + 1] + MAGIC_BITS), MAGIC);
-            const float p0 = __fmul_rn(f0, __fmul_rn(w, xv[j])), p1 = __fmul_rn(f1, __fmul_rn(w, xv[j + 1]));
-            accp[(c + i + j) / 2] = pack2(__fadd_rn(lo(a), p0), __fadd_rn(hi(a), p1));
+        for (int j = 0; j < 4; j++) {
+          const int g = 4 * k + j;
+          if (j < groups) {
+            // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
+            const float f = __fsub_rn(__uint_as_float(v[j][t] + MAGIC_BITS), MAGIC);
+            const float p = __fmul_rn(f, __fmul_rn(wv[j], xv[j]));
+            if (g < ng4) {
+              acc[t][j] = __fadd_rn(acc[t][j], p);  // lane g % 4 (= j: stages hold four groups)
+            } else {
+              if (g == ng4)  // the lanes added in order before the groups past the fours (kernel_relaxed.ts:57)
+                acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
+              acc[t][0] = __fadd_rn(acc[t][0], p);  // kernel_relaxed.ts:58-64
+            }
           }
         }
       }
-    };
-    for (int g = chain; g < ng4; g += 4) group(g, acc);
-    // the chain lanes meet: 1..3 hand theirs to lane 0's warp of the same quarter
-    if (chain > 0) {
-#pragma unroll
-      for (int i = 0; i < BN / 2; i++) {
-        s.comb[chain - 1][2 * i][quarter * 32 + lane] = lo(acc[i]);
-        s.comb[chain - 1][2 * i + 1][quarter * 32 + lane] = hi(acc[i]);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[st]);
     }
-    named_sync(5 + quarter, 128);
-    if (chain == 0) {
-      // ((lane 0 + lane 1) + lane 2) + lane 3
+    if (ng4 == ng)
 #pragma unroll
-      for (int i = 0; i < BN / 2; i++) {
-        uint64_t v = acc[i];
-        for (int c = 0; c < 3; c++)
-          v = add2(v, pack2(s.comb[c][2 * i][quarter * 32 + lane], s.comb[c][2 * i + 1][quarter * 32 + lane]));
-        acc[i] = v;
-      }
-      // the groups past the fours, one at a time
-      for (int g = ng4; g < ng; g++) group(g, acc);
-      if (r < args.rows) {
-        float *out = args.out + r;
+      for (int t = 0; t < TPW; t++)
+        acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
+    const int r = row0 + rl;
+    if (r < args.rows) {
 #pragma unroll
-        for (int i = 0; i < BN / 2; i++) {
-          const int t = tok0 + 2 * i;
-          if (t < args.count) {
-            float *o = out + (int64_t)t * args.out_stride;
-            *o = args.accumulate ? __fadd_rn(*o, lo(acc[i])) : lo(acc[i]);
-          }
-          if (t + 1 < args.count) {
-            float *o = out + (int64_t)(t + 1) * args.out_stride;
-            *o = args.accumulate ? __fadd_rn(*o, hi(acc[i])) : hi(acc[i]);
-          }
+      for (int t = 0; t < TPW; t++) {
+        const int tok = tok0 + sub * TPW + t;
+        if (tok < args.count) {
+          float *o = args.out + (int64_t)tok * args.out_stride + r;
+          *o = args.accumulate ? __fadd_rn(*o, acc[t][0]) : acc[t][0];
         }
       }
     }
@@ -344,26 +350,37 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t row_bytes, int box_rows) {
+int make_map(CUtensorMap *map, CUtensorMapDataType type, int esize, const void *base, int64_t cols, int64_t rows,
+             int64_t row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return fail(B200FWD_ECUDA, "cuTensorMapEncodeTiled is not available");
   if (reinterpret_cast<uintptr_t>(base) % 16 || row_bytes % 16)
     return fail(B200FWD_EINVAL, "a TMA tensor must start on, and have rows of, multiples of 16 bytes");
+  if (cols < box_cols || rows < box_rows) return fail(B200FWD_EINVAL, "a TMA box larger than its tensor");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  cuuint32_t box[2] = {(cuuint32_t)KSTAGE, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t elem[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, elem,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, type, 2, const_cast<void *>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(B200FWD_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  (void)esize;
   return 0;
+}
+
+int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t row_bytes, int box_rows) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, cols, rows, row_bytes, KSTAGE, box_rows,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int make_scale_map(CUtensorMap *map, const float *base, int64_t groups, int64_t rows, int64_t row_floats, int box_rows) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, groups, rows, row_floats * 4, 4, box_rows,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 size_t gemm_smem_bytes() { return sizeof(Smem) + 1024; }
 
-int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmArgs &args, int bn,
-                   cudaStream_t stream) {
+int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream) {
   if (args.count <= 0 || args.rows <= 0) return 0;
   if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
   if (bn != 16 && bn != 32) return fail(B200FWD_EINVAL, "gemm: BN must be 16 or 32");
@@ -378,9 +395,9 @@ int launch_gemm_tc(const CUtensorMap &wmap, const CUtensorMap &xmap, const GemmA
     if (bit) opted.fetch_or(bit);
   }
   if (bn == 16)
-    q8_gemm_tc<16><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+    q8_gemm_tc<16><<<grid, THREADS, smem, stream>>>(maps.w, maps.x, maps.ws, maps.xs, args);
   else
-    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(wmap, xmap, args);
+    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(maps.w, maps.x, maps.ws, maps.xs, args);
   B200_LAUNCHED("q8_gemm_tc");
   return 0;
 }

@@ -81,9 +81,11 @@ __global__ void __launch_bounds__(MV_WARPS * 32)
       }
     }
     const int8_t *wrow = pick3(j, jobs.job[0].w, jobs.job[1].w, jobs.job[2].w) + (int64_t)r * n;
-    const float *srow = pick3(j, jobs.job[0].s, jobs.job[1].s, jobs.job[2].s) + (int64_t)r * ng;
+    const int ss = pick3(j, jobs.job[0].sstride, jobs.job[1].sstride, jobs.job[2].sstride);
+    const int64_t sstride = ss ? ss : ng;
+    const float *srow = pick3(j, jobs.job[0].s, jobs.job[1].s, jobs.job[2].s) + (int64_t)r * sstride;
     const int32_t *cbase = pick3(j, jobs.job[0].c, jobs.job[1].c, jobs.job[2].c);
-    const int32_t *crow = cbase ? cbase + (int64_t)r * ng : nullptr;
+    const int32_t *crow = cbase ? cbase + (int64_t)r * sstride : nullptr;
     float *out = pick3(j, jobs.job[0].out, jobs.job[1].out, jobs.job[2].out) + r;
     const int64_t ostride = pick3(j, jobs.job[0].out_stride, jobs.job[1].out_stride, jobs.job[2].out_stride);
     const int accumulate = pick3(j, jobs.job[0].accumulate, jobs.job[1].accumulate, jobs.job[2].accumulate);
@@ -261,13 +263,13 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
   quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
 }
 
-__global__ void embed_kernel(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim,
+__global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
                              float *x, int64_t x_stride) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)count * dim) return;
   const int t = (int)(i / dim), j = (int)(i % dim);
-  const int64_t at = (int64_t)tokens[t] * dim + j;
-  x[(int64_t)t * x_stride + j] = fmul((float)w[at], s[at / group]);
+  const int64_t row = tokens[t];
+  x[(int64_t)t * x_stride + j] = fmul((float)w[row * dim + j], s[row * sstride + j / 32]);
 }
 
 __global__ void rope_cache_kernel(float *q, int64_t q_stride, const float *k, const float *v, int64_t kv_stride,
@@ -527,14 +529,13 @@ __global__ void gather_rows_kernel(float *dst, int64_t dst_stride, const float *
   dst[(int64_t)t * dst_stride + j] = src[(int64_t)idx[t] * src_stride + j];
 }
 
-__global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+__global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                                        const int32_t *channels, int nch) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)vocab * nch) return;
   const int c = (int)(i / vocab), v = (int)(i % vocab);
   const int ch = channels[c];
-  const int groups = dim / group;
-  cols[i] = fmul((float)w[(int64_t)v * dim + ch], s[(int64_t)v * groups + ch / group]);
+  cols[i] = fmul((float)w[(int64_t)v * dim + ch], s[(int64_t)v * sstride + ch / 32]);
 }
 
 __global__ void to_f16_kernel(uint16_t *out, const float *x, int64_t n) {
@@ -650,10 +651,10 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
   return 0;
 }
 
-int launch_embed(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim, float *x,
+int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim, float *x,
                  int64_t x_stride, cudaStream_t stream) {
   if (count <= 0) return 0;
-  embed_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(w, s, group, tokens, count, dim, x,
+  embed_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(w, s, sstride, tokens, count, dim, x,
                                                                           x_stride);
   B200_LAUNCHED("embed_kernel");
   return 0;
@@ -759,10 +760,10 @@ int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t
   return 0;
 }
 
-int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                            const int32_t *channels, int nch, cudaStream_t stream) {
   if (nch <= 0) return 0;
-  outlier_columns_kernel<<<blocks_for((int64_t)vocab * nch, 256), 256, 0, stream>>>(cols, w, s, group, dim, vocab,
+  outlier_columns_kernel<<<blocks_for((int64_t)vocab * nch, 256), 256, 0, stream>>>(cols, w, s, sstride, dim, vocab,
                                                                                      channels, nch);
   B200_LAUNCHED("outlier_columns_kernel");
   return 0;

@@ -19,6 +19,7 @@ struct MatJob {
   int rows;
   int accumulate;     // out += the result (the residual add of forward.js:500,519), else out = the result
   int64_t out_stride;
+  int sstride;        // scales (and corrections) per row; 0: n / 32
 };
 struct MatJobs {
   MatJob job[3];
@@ -46,8 +47,8 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
 // kernel.ts:654-667 swiglu then quantize_x of its output, per token
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
                            int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream, int shift = 0);
-// forward.js:403-414 embed of int8 rows: x[t][i] = w[token*dim+i] * s[(token*dim+i)/group]; tokens on the device
-int launch_embed(const int8_t *w, const float *s, int group, const int32_t *tokens, int count, int dim, float *x,
+// forward.js:403-414 embed of int8 rows: x[t][i] = w[token*dim+i] * s[token*sstride + i/32]; tokens on the device
+int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim, float *x,
                  int64_t x_stride, cudaStream_t stream);
 // forward.js:489-494: rope (kernel.ts:344-357) on q and k of each token at its position, and k, v into its
 // sequence's cache (to_f16 when half). cache of sequence s: kc + s * seq_stride elements, [pos][nkv*hs]
@@ -71,8 +72,8 @@ int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count
 // dst[i] = src[idx[i]] (rows of dim floats)
 int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t src_stride, const int32_t *idx,
                        int count, int dim, cudaStream_t stream);
-// forward.js:799-813 the outlier channels' float32 columns: cols[i][v] = w[v*dim+c_i] * s[v*groups + c_i/group]
-int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int group, int dim, int vocab,
+// forward.js:799-813 the outlier channels' float32 columns: cols[i][v] = w[v*dim+c_i] * s[v*sstride + c_i/32]
+int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                            const int32_t *channels, int nch, cudaStream_t stream);
 int launch_to_f16(uint16_t *out, const float *x, int64_t n, cudaStream_t stream);
 int launch_from_f16(float *out, const uint16_t *x, int64_t n, cudaStream_t stream);

@@ -112,22 +112,30 @@ def test_matmul_q8r_large_random(lib):
 
 
 def matmul_signed(lib, xq7, xs, w, ws, n, count):
-    """b200k_matmul_q8s: activations of quantize_x(bias 64) handed over less the bias."""
+    """b200k_matmul_q8s: activations of quantize_x(bias 64) handed over less the bias; scale rows padded to a
+    multiple of four floats (the tensor cores' TMA rows), as the engine keeps them."""
     rows = w.size // n
+    ng = n // 32
+    ngp = (ng + 3) // 4 * 4
     qs = ((n + 15) // 16) * 16
     xsg = np.zeros((count, qs), np.int8)
     xsg[:, :n] = (xq7[:count].astype(np.int16) - 64).astype(np.int8)
-    dq, ds, dw, dws = dev(xsg), dev(np.ascontiguousarray(xs[:count], np.float32)), dev(w), dev(ws)
+    xsp = np.zeros((count, ngp), np.float32)
+    xsp[:, :ng] = xs[:count, :ng]
+    wsp = np.zeros((rows, ngp), np.float32)
+    wsp[:, :ng] = ws.reshape(rows, ng)
+    dq, ds, dw, dws = dev(xsg), dev(xsp), dev(w), dev(wsp)
     out = full((count, rows), -7.0)
-    abi.check(lib.b200k_matmul_q8s(ptr(out), ptr(dq), ptr(ds), ptr(dw), ptr(dws), n, rows, count, rows, qs,
-                                   xs.shape[1], None))
+    abi.check(lib.b200k_matmul_q8s(ptr(out), ptr(dq), ptr(ds), ptr(dw), ptr(dws), ngp, n, rows, count, rows, qs, ngp,
+                                   None))
     return host(out)
 
 
-@pytest.mark.parametrize("n,rows", [(4096, 6144), (14336, 300), (288, 768), (160, 64), (4096, 1024)])
+@pytest.mark.parametrize("n,rows", [(4096, 6144), (14336, 300), (288, 768), (160, 200), (4096, 1024), (4096, 64)])
 def test_matmul_tensor_cores(lib, n, rows):
     """The tensor-core path (count >= 16 tokens) to the bit against the oracle's matmul_q8r, at the 8B and stories
-    shapes and at widths with groups past the fours (288: 9 groups; 160: 5), every token tile width."""
+    shapes and at widths with groups past the fours (288: 9 groups; 160: 5), both token tile widths; 64 rows take
+    the CUDA cores."""
     rng = np.random.default_rng(n + rows)
     w = rng.integers(-128, 128, size=rows * n, dtype=np.int8)
     w[:32] = -128

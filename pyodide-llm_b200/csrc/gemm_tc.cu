@@ -48,11 +48,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // true when the phase of `parity` completed; false when the wait gave up, or another warp of the grid already did
-// (the error flag is then set and every later wait returns at once: the kernel runs to its end and frees TMEM)
+// (the error flag is then set and every later wait returns soon: the kernel runs to its end and frees TMEM). The
+// error word (global memory) is read only every 1024 unsuccessful tries, never on the way of a ready barrier.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *error, int code) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-    if (*(volatile int *)error) return false;
+  for (uint32_t i = 0;; i++) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -62,9 +62,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 1023) == 1023) {
+      if (*(volatile int *)error) return false;
+      if (i >= WAIT_LIMIT) {
+        atomicCAS(error, 0, code);
+        return false;
+      }
+    }
   }
-  atomicCAS(error, 0, code);
-  return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {

@@ -32,7 +32,8 @@ constexpr int STAGES = 8;
 constexpr int BN_MAX = 32;            // tokens of a tile at most (32 accumulators a thread)
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr uint32_t WAIT_HINT_NS = 1000000;  // 1 ms
+constexpr uint32_t WAIT_TRIES = 2000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -48,26 +49,26 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // true when the phase of `parity` completed; false when the wait gave up, or another warp of the grid already did
-// (the error flag is then set and every later wait returns soon: the kernel runs to its end and frees TMEM). The
-// error word (global memory) is read only every 1024 unsuccessful tries, never on the way of a ready barrier.
+// (the error flag is then set and every later wait returns soon: the kernel runs to its end and frees TMEM).
+// try_wait with a suspend-time hint: a waiting warp sleeps until the phase completes (it takes no issue slots from
+// the producer and MMA warps) or the hint's 1 ms passes; the error word (global memory) is read only then, and
+// after WAIT_TRIES such expiries (about 2 s) the wait gives up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *error, int code) {
   const uint32_t addr = smem_u32(bar);
   for (uint32_t i = 0;; i++) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(WAIT_HINT_NS)
         : "memory");
     if (done) return true;
-    if ((i & 1023) == 1023) {
-      if (*(volatile int *)error) return false;
-      if (i >= WAIT_LIMIT) {
-        atomicCAS(error, 0, code);
-        return false;
-      }
+    if (*(volatile int *)error) return false;
+    if (i >= WAIT_TRIES) {
+      atomicCAS(error, 0, code);
+      return false;
     }
   }
 }

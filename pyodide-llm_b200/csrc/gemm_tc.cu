@@ -259,6 +259,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---- epilogue
     const int quarter = warp % 4, sub = (warp - 2) / 4;
+    const uint32_t magic_bits = args.magic_bits;
+    const float magic = args.magic;
     const int rl = quarter * 32 + lane;  // the row within the tile
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
     float acc[TPW][4];
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int g = 4 * k + j;
           if (j < groups) {
             // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
-            const float f = __fsub_rn(__uint_as_float(v[j][t] + MAGIC_BITS), MAGIC);
+            const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
             const float p = __fmul_rn(f, __fmul_rn(wv[j], xv[j]));
             if (g < ng4) {
               acc[t][j] = __fadd_rn(acc[t][j], p);  // lane g % 4 (= j: stages hold four groups)
@@ -386,7 +388,10 @@ int make_scale_map(CUtensorMap *map, const float *base, int64_t groups, int64_t 
 
 size_t gemm_smem_bytes() { return sizeof(Smem) + 1024; }
 
-int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream) {
+int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &given, int bn, cudaStream_t stream) {
+  GemmArgs args = given;
+  args.magic_bits = MAGIC_BITS;
+  args.magic = MAGIC;
   if (args.count <= 0 || args.rows <= 0) return 0;
   if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
   if (bn != 16 && bn != 32) return fail(B200FWD_EINVAL, "gemm: BN must be 16 or 32");

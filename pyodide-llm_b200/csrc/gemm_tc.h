@@ -14,6 +14,11 @@ struct GemmArgs {
   int w_row0;        // this matrix's first row in the weight view (a layer's offset)
   int64_t out_stride;
   int accumulate;    // out += result
+  // 0x4B400000 and 12582912.0f, handed over at run time: an int32 S below 2^22 in magnitude is float(S) exactly
+  // as (the float with bits S + magic_bits) - magic. (As literals the compiler turns the pair back into a
+  // conversion instruction, a far slower pipe.)
+  uint32_t magic_bits;
+  float magic;
 };
 
 // the four TMA maps of one matmul

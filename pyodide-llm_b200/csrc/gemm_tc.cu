@@ -158,7 +158,7 @@ struct Smem {
   alignas(128) float ws[STAGES][BM][4];               // the rows' four groups' scales
   alignas(128) float xs[STAGES][BN_MAX][4];           // the tokens' four groups' scales
   uint64_t full[STAGES], empty[STAGES];
-  uint64_t slot_full[32], slot_empty[32];
+  uint64_t slot_full[8], slot_empty[8];  // TMEM stage slots: four groups' columns each
   uint32_t tmem_base;
 };
 
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap, GemmArgs args) {
   extern __shared__ uint8_t raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-  constexpr int SLOTS = 512 / BN;
+  constexpr int SLOTS = 512 / (4 * BN);  // TMEM holds this many stages' four groups at once
   constexpr int TPW = BN / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = args.n >> 5, ng4 = ng & ~3;
@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1 + EPI_WARPS);  // the MMAs' commit, and every epilogue warp done with the scales
+      // every epilogue warp done with the stage (it has seen the stage's MMAs complete, so A and B are free too)
+      mbar_init(&s.empty[i], EPI_WARPS);
     }
     for (int i = 0; i < SLOTS; i++) {
       mbar_init(&s.slot_full[i], 1);
@@ -230,31 +231,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issue: one MMA per group into its slot
+    // ---- MMA issue: a stage's four groups, one MMA each (K = 32, one group) into four TMEM column blocks of the
+    // stage's slot, one commit per stage
     const uint32_t idesc = idesc_i8(BN);
     for (int k = 0; k < kstages; k++) {
-      const int st = k % STAGES;
+      const int st = k % STAGES, slot = k % SLOTS;
       if (!mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 2)) break;
+      if (!mbar_wait(&s.slot_empty[slot], ((k / SLOTS) & 1) ^ 1, args.error, 3)) break;
       tc_fence_after();
-      bool ok = true;
-      for (int j = 0; j < 4; j++) {
-        const int g = k * 4 + j;
-        if (g >= ng) break;
-        const int slot = g % SLOTS;
-        if (!mbar_wait(&s.slot_empty[slot], ((g / SLOTS) & 1) ^ 1, args.error, 3)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          mma_i8(tmem + (uint32_t)(slot * BN), smem_desc(s.a[st] + 32 * j), smem_desc(s.b[st] + 32 * j), idesc);
-          mma_commit(&s.slot_full[slot]);
-        }
-        __syncwarp();
+      if (lane == 0) {
+        const int groups = min(4, ng - 4 * k);
+        for (int j = 0; j < groups; j++)
+          mma_i8(tmem + (uint32_t)((slot * 4 + j) * BN), smem_desc(s.a[st] + 32 * j), smem_desc(s.b[st] + 32 * j),
+                 idesc);
+        mma_commit(&s.slot_full[slot]);
       }
-      if (lane == 0) mma_commit(&s.empty[st]);
       __syncwarp();
-      if (!ok) break;
     }
   } else {
     // ---- epilogue
@@ -272,41 +264,45 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int st = k % STAGES;
       mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 4);
       const int groups = min(4, ng - 4 * k);
-      // the stage's groups' sums of this warp's tokens, then its slots go back to the MMAs
+      // the stage's groups' sums of this warp's tokens, then the stage's slot goes back to the MMAs
+      const int slot = k % SLOTS;
+      mbar_wait(&s.slot_full[slot], (k / SLOTS) & 1, args.error, 5);
+      tc_fence_after();
       uint32_t v[4][TPW];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        if (j < groups) {
-          const int g = 4 * k + j, slot = g % SLOTS;
-          mbar_wait(&s.slot_full[slot], (g / SLOTS) & 1, args.error, 5);
-          tc_fence_after();
-          tmem_ld<TPW>(taddr + (uint32_t)(slot * BN), v[j]);
-        }
-      }
+      for (int j = 0; j < 4; j++)
+        if (j < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), v[j]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0)
-        for (int j = 0; j < groups; j++) mbar_arrive(&s.slot_empty[(4 * k + j) % SLOTS]);
+      if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
       const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
       const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      if (4 * k + 4 <= ng4) {
+        // a whole stage below the last four: lane j of the chain takes group 4k + j, no branch in between
 #pragma unroll
-      for (int t = 0; t < TPW; t++) {
-        const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
-        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+        for (int t = 0; t < TPW; t++) {
+          const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
+          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int g = 4 * k + j;
-          if (j < groups) {
+          for (int j = 0; j < 4; j++) {
             // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
             const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
-            const float p = __fmul_rn(f, __fmul_rn(wv[j], xv[j]));
-            if (g < ng4) {
-              acc[t][j] = __fadd_rn(acc[t][j], p);  // lane g % 4 (= j: stages hold four groups)
-            } else {
-              if (g == ng4)  // the lanes added in order before the groups past the fours (kernel_relaxed.ts:57)
-                acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
-              acc[t][0] = __fadd_rn(acc[t][0], p);  // kernel_relaxed.ts:58-64
+            acc[t][j] = __fadd_rn(acc[t][j], __fmul_rn(f, __fmul_rn(wv[j], xv[j])));
+          }
+        }
+      } else {
+        // the stage with the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
+#pragma unroll
+        for (int t = 0; t < TPW; t++) {
+          const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
+          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+          acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            if (j < groups) {
+              const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
+              acc[t][0] = __fadd_rn(acc[t][0], __fmul_rn(f, __fmul_rn(wv[j], xv[j])));
             }
           }
         }

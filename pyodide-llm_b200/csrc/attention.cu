@@ -1,0 +1,339 @@
+// attention.cu — kernel.ts:447-566 attentionOf (attention / attention_f16) for many query tokens at once, each to the
+// bit as the reference computes it alone, with the keys and values staged through shared memory.
+//
+// Query tokens come in tiles: up to ATT_TT consecutive tokens of one sequence at consecutive positions (a prompt
+// block), or a single token (decode). A tile shares its sequence's keys and values, so every block loads a chunk of
+// ATT_CH positions once with coalesced 16-byte loads, widens it exactly to float32 (the reference's half(), the
+// 2^112 multiply) in shared memory, and serves every token and every query head of the kv head from it.
+//
+//   scores  grid (chunks, kv heads, tiles), a thread a position: per token and head four lane accumulators over
+//           the head's fours, (l0+l2)+(l1+l3), the rest after, times 1/sqrt(hs) (kernel.ts:462-498);
+//   softmax grid (heads, tokens): the largest, exp (vexp on the fours, fexp after), four lane sums then the rest,
+//           times 1/sum (kernel.ts:499-521);
+//   values  grid (kv heads, tiles), a thread two neighbouring values of one head for every token of the tile: the
+//           positions in fours ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) added in order, then the positions past the
+//           fours one by one (kernel.ts:522-565); values past the fours of a head add their four products one after
+//           another.
+#include <algorithm>
+#include <cfloat>
+#include <cstdint>
+
+#include "common.h"
+#include "exact.cuh"
+#include "kernels.h"
+
+namespace b200 {
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int ATT_CH = 64;   // positions of a chunk
+constexpr int ATT_TT = 16;   // tokens of a tile at most
+constexpr size_t MAX_SOFTMAX_SMEM = 200 * 1024;
+constexpr size_t MAX_TILE_SMEM = 200 * 1024;
+
+#define CHECK_ATT(expr)  \
+  do {                   \
+    int rc_ = (expr);    \
+    if (rc_) return rc_; \
+  } while (0)
+
+struct Tile {
+  int first, count;
+};
+
+__device__ __forceinline__ Tile tile_of(const int32_t *tiles, int i) {
+  if (tiles) return Tile{tiles[2 * i], tiles[2 * i + 1]};
+  return Tile{i, 1};
+}
+__device__ __forceinline__ int pos_of(const int32_t *pos, int pos0, int tok) { return pos ? pos[tok] : pos0; }
+
+// positions c0..c0+rows-1 of one kv head of one sequence's cache, as float32, into dst rows `pitch` floats apart
+template <bool HALF>
+__device__ __forceinline__ void stage_rows(float *dst, int pitch, const void *cache, int64_t row0, int64_t kvDim,
+                                           int hs, int rows, bool vec) {
+  if (vec) {
+    constexpr int per = HALF ? 8 : 4;  // values a 16-byte load holds
+    const int pieces = hs / per;
+    for (int idx = threadIdx.x; idx < rows * pieces; idx += blockDim.x) {
+      const int r = idx / pieces, p = idx % pieces;
+      const int64_t at = row0 + (int64_t)r * kvDim + p * per;
+      float *d = dst + r * pitch + p * per;
+      if (HALF) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(cache) + at);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          d[2 * k] = half_to_float((uint16_t)(w[k] & 0xffff));
+          d[2 * k + 1] = half_to_float((uint16_t)(w[k] >> 16));
+        }
+      } else {
+        const float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(cache) + at);
+        d[0] = f.x;
+        d[1] = f.y;
+        d[2] = f.z;
+        d[3] = f.w;
+      }
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < rows * hs; idx += blockDim.x) {
+      const int r = idx / hs, j = idx % hs;
+      const int64_t at = row0 + (int64_t)r * kvDim + j;
+      dst[r * pitch + j] = HALF ? half_to_float(reinterpret_cast<const uint16_t *>(cache)[at])
+                                : reinterpret_cast<const float *>(cache)[at];
+    }
+  }
+}
+
+template <bool HALF, int G>
+__global__ void __launch_bounds__(ATT_CH)
+    attn_scores_tiled(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
+                      const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
+                      int hs, int h0, int h1, int vec) {
+  extern __shared__ float sm[];
+  const int kvh = blockIdx.y, chunk = blockIdx.x;
+  const Tile tl = tile_of(tiles, blockIdx.z);
+  const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
+  const int c0 = chunk * ATT_CH;
+  if (c0 > last) return;
+  const int rows = min(ATT_CH, last + 1 - c0);
+  const int kvDim = nkv * hs, hs4 = hs & ~3, hsp = (hs + 3) & ~3, pitch = hsp + 4;
+  float *kf = sm;                        // [ATT_CH][pitch]: rows on 16 bytes, banks apart
+  float *qs = sm + ATT_CH * pitch;       // [count][G][hsp]
+  const int64_t sq = seq ? seq[tl.first] : 0;
+  stage_rows<HALF>(kf, pitch, kc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs, kvDim, hs, rows, vec);
+  for (int idx = threadIdx.x; idx < tl.count * G * hs; idx += blockDim.x) {
+    const int i = idx / (G * hs), r = idx % (G * hs), gg = r / hs, d = r % hs;
+    qs[(i * G + gg) * hsp + d] = q[(int64_t)(tl.first + i) * q_stride + (int64_t)kvh * G * hs + r];
+  }
+  __syncthreads();
+  const int t = threadIdx.x, p = c0 + t;
+  if (t >= rows) return;
+  const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
+  const float *krow = kf + t * pitch;
+  for (int i = 0; i < tl.count; i++) {
+    const int tok = tl.first + i;
+    if (p > pos_of(pos, pos0, tok)) continue;  // causal: a token reads the positions up to its own
+    float a[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++) a[g][0] = a[g][1] = a[g][2] = a[g][3] = 0.0f;
+    const float *qi = qs + i * G * hsp;
+    for (int j = 0; j < hs4; j += 4) {
+      const float4 k4 = *reinterpret_cast<const float4 *>(krow + j);
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(qi + g * hsp + j);
+        a[g][0] = fadd(a[g][0], fmul(q4.x, k4.x));
+        a[g][1] = fadd(a[g][1], fmul(q4.y, k4.y));
+        a[g][2] = fadd(a[g][2], fmul(q4.z, k4.z));
+        a[g][3] = fadd(a[g][3], fmul(q4.w, k4.w));
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const int h = kvh * G + g;
+      if (h < h0 || h >= h1) continue;
+      float s = fadd(fadd(a[g][0], a[g][2]), fadd(a[g][1], a[g][3]));
+      for (int j = hs4; j < hs; j++) s = fadd(s, fmul(qi[g * hsp + j], krow[j]));
+      att[((int64_t)tok * nh + h) * P + p] = fmul(s, isq);
+    }
+  }
+}
+
+__global__ void attn_softmax_tiled(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1) {
+  extern __shared__ float e[];
+  __shared__ float part[5];
+  __shared__ float wm[32];
+  const int tok = blockIdx.y, h = blockIdx.x;
+  if (h < h0 || h >= h1) return;
+  const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
+  float *row = att + ((int64_t)tok * nh + h) * P;
+  // the largest from -FLT_MAX, a NaN kept (kernel.ts:423-445: the order does not matter)
+  float mx = -FLT_MAX;
+  for (int t = threadIdx.x; t < count; t += blockDim.x) mx = wmax(mx, row[t]);
+  for (int o = 16; o > 0; o >>= 1) mx = wmax(mx, __shfl_xor_sync(FULL, mx, o));
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -FLT_MAX;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = wmax(mx, wm[w]);
+  for (int t = threadIdx.x; t < count; t += blockDim.x) {
+    const float d = fsub(row[t], mx);
+    e[t] = t < count4 ? vexp(d) : fexp(d);
+  }
+  __syncthreads();
+  if (threadIdx.x < 4) {
+    float acc = 0.0f;
+    for (int t = threadIdx.x; t < count4; t += 4) acc = fadd(acc, e[t]);
+    part[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
+    for (int t = count4; t < count; t++) sum = fadd(sum, e[t]);
+    part[4] = fdiv(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = part[4];
+  for (int t = threadIdx.x; t < count; t += blockDim.x) row[t] = fmul(e[t], inv);
+}
+
+// one output value's step over four positions (kernel.ts:535-545): below the head's fours the products in pairs,
+// past them one after another
+__device__ __forceinline__ float four(float o, float w0, float w1, float w2, float w3, float v0, float v1, float v2,
+                                      float v3, bool in_fours) {
+  if (in_fours) return fadd(o, fadd(fadd(fmul(w0, v0), fmul(w1, v1)), fadd(fmul(w2, v2), fmul(w3, v3))));
+  return fadd(fadd(fadd(fadd(o, fmul(w0, v0)), fmul(w1, v1)), fmul(w2, v2)), fmul(w3, v3));
+}
+
+template <bool HALF, int G>
+__global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc, const float *att,
+                                  const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles,
+                                  int64_t seq_stride, int P, int nh, int nkv, int hs, int h0, int h1, int vec) {
+  extern __shared__ float sm[];
+  const int kvh = blockIdx.x;
+  const Tile tl = tile_of(tiles, blockIdx.y);
+  const int kvDim = nkv * hs, hs4 = hs & ~3, hp = (hs + 1) / 2;
+  float *vs = sm;                      // [ATT_CH][hs]
+  float *wsm = sm + ATT_CH * hs;       // [count][G][ATT_CH]
+  const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
+  const int h = kvh * G + g;
+  const bool active = g < G && h >= h0 && h < h1;
+  const int j0 = 2 * jp, j1 = j0 + 1;
+  const bool has1 = j1 < hs;
+  const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
+  const int64_t sq = seq ? seq[tl.first] : 0;
+  float o0[ATT_TT], o1[ATT_TT];
+#pragma unroll
+  for (int i = 0; i < ATT_TT; i++) o0[i] = o1[i] = 0.0f;
+  for (int c0 = 0; c0 <= last; c0 += ATT_CH) {
+    const int rows = min(ATT_CH, last + 1 - c0);
+    __syncthreads();  // the previous chunk is done with
+    stage_rows<HALF>(vs, hs, vc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs, kvDim, hs, rows, vec);
+    for (int idx = threadIdx.x; idx < tl.count * G * ATT_CH; idx += blockDim.x) {
+      const int i = idx / (G * ATT_CH), r = idx % (G * ATT_CH), gg = r / ATT_CH, p = r % ATT_CH;
+      const int tok = tl.first + i, hh = kvh * G + gg;
+      float w = 0.0f;
+      if (p < rows && c0 + p <= pos_of(pos, pos0, tok) && hh >= h0 && hh < h1)
+        w = att[((int64_t)tok * nh + hh) * P + c0 + p];
+      wsm[idx] = w;
+    }
+    __syncthreads();
+    if (!active) continue;
+    for (int p = 0; p < rows; p += 4) {
+      const int P0 = c0 + p;
+      const int n4 = min(4, rows - p);
+      float v0[4], v1[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        v0[u] = u < n4 ? vs[(p + u) * hs + j0] : 0.0f;
+        v1[u] = (u < n4 && has1) ? vs[(p + u) * hs + j1] : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < ATT_TT; i++) {
+        if (i >= tl.count) break;
+        const int count = pos_of(pos, pos0, tl.first + i) + 1, count4 = count & ~3;
+        const float *w = wsm + (i * G + g) * ATT_CH + p;
+        if (P0 + 4 <= count4) {
+          const float4 w4 = *reinterpret_cast<const float4 *>(w);
+          o0[i] = four(o0[i], w4.x, w4.y, w4.z, w4.w, v0[0], v0[1], v0[2], v0[3], j0 < hs4);
+          if (has1) o1[i] = four(o1[i], w4.x, w4.y, w4.z, w4.w, v1[0], v1[1], v1[2], v1[3], j1 < hs4);
+        } else if (P0 < count) {
+          // the positions past the fours, one at a time (kernel.ts:548-564)
+          for (int u = 0; u < 4 && P0 + u < count; u++) {
+            o0[i] = fadd(o0[i], fmul(w[u], v0[u]));
+            if (has1) o1[i] = fadd(o1[i], fmul(w[u], v1[u]));
+          }
+        }
+      }
+    }
+  }
+  if (!active) return;
+#pragma unroll
+  for (int i = 0; i < ATT_TT; i++) {
+    if (i >= tl.count) break;
+    float *o = out + (int64_t)(tl.first + i) * out_stride + h * hs;
+    o[j0] = o0[i];
+    if (has1) o[j1] = o1[i];
+  }
+}
+
+template <bool HALF, int G>
+int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
+                 float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
+                 int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int vec,
+                 cudaStream_t stream) {
+  const int chunks = (max_count + ATT_CH - 1) / ATT_CH;
+  const int tt = tiles ? ATT_TT : 1;
+  const int hsp = (hs + 3) & ~3;
+  const size_t smem_scores = (size_t)(ATT_CH * (hsp + 4) + tt * G * hsp) * sizeof(float);
+  const size_t smem_values = (size_t)(ATT_CH * hs + tt * G * ATT_CH) * sizeof(float);
+  if (smem_scores > MAX_TILE_SMEM || smem_values > MAX_TILE_SMEM)
+    return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a tile in shared memory");
+  B200_CUDA(cudaFuncSetAttribute(attn_scores_tiled<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)MAX_TILE_SMEM));
+  B200_CUDA(cudaFuncSetAttribute(attn_values_tiled<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)MAX_TILE_SMEM));
+  attn_scores_tiled<HALF, G><<<dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream>>>(
+      q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
+  B200_LAUNCHED("attn_scores_tiled");
+  const size_t smem_soft = (size_t)max_count * sizeof(float);
+  if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
+  attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
+  B200_LAUNCHED("attn_softmax_tiled");
+  const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
+  attn_values_tiled<HALF, G><<<dim3(nkv, ntiles), threads, smem_values, stream>>>(
+      out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
+  B200_LAUNCHED("attn_values_tiled");
+  return 0;
+}
+
+}  // namespace
+
+int prepare_attention() {
+  int device = 0;
+  B200_CUDA(cudaGetDevice(&device));
+  static std::atomic<uint64_t> opted{0};
+  if (device >= 64 || !(opted.load() & (1ull << device))) {
+    B200_CUDA(cudaFuncSetAttribute(attn_softmax_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)MAX_SOFTMAX_SMEM));
+    if (device < 64) opted.fetch_or(1ull << device);
+  }
+  return 0;
+}
+
+int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
+                     float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
+                     int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1,
+                     int half, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  if (nkv <= 0 || nh % nkv) return fail(B200FWD_EINVAL, "attention: heads must be a multiple of the kv heads");
+  if (max_count > P) return fail(B200FWD_EINVAL, "attention: a position past the scratch");
+  if (!tiles) ntiles = count;
+  CHECK_ATT(prepare_attention());
+  // 16-byte loads where every row of the head starts on 16 bytes
+  const int esize = half ? 2 : 4, per = half ? 8 : 4;
+  const int vec = hs % per == 0 && (nkv * hs * esize) % 16 == 0 && reinterpret_cast<uintptr_t>(kc) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(vc) % 16 == 0 && (seq_stride * esize) % 16 == 0;
+  const int G = nh / nkv;
+#define B200_ATT(H, GG)                                                                                            \
+  return launch_tiled<H, GG>(out, out_stride, q, q_stride, kc, vc, att, seq, pos, pos0, tiles, ntiles, count,     \
+                             seq_stride, P, max_count, nh, nkv, hs, h0, h1, vec, stream)
+  if (half) {
+    switch (G) {
+      case 1: B200_ATT(true, 1);
+      case 2: B200_ATT(true, 2);
+      case 4: B200_ATT(true, 4);
+      case 8: B200_ATT(true, 8);
+    }
+  } else {
+    switch (G) {
+      case 1: B200_ATT(false, 1);
+      case 2: B200_ATT(false, 2);
+      case 4: B200_ATT(false, 4);
+      case 8: B200_ATT(false, 8);
+    }
+  }
+#undef B200_ATT
+  return fail(B200FWD_EUNSUPPORTED, "attention: query heads per kv head must be 1, 2, 4 or 8");
+}
+
+}  // namespace b200

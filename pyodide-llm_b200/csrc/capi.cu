@@ -151,8 +151,8 @@ int b200k_attention(float *out, const float *q, const void *kc, const void *vc, 
     if (pos < 0 || nh < 1 || nkv < 1 || nh % nkv || hs < 1 || h0 < 0 || h1 > nh || h0 > h1)
       return fail(B200FWD_EINVAL, "attention: bad sizes");
     if (h0 == h1) return 0;
-    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, nullptr, nullptr, pos, 1, 0, pos + 1, pos + 1, nh,
-                            nkv, hs, h0, h1, half ? 1 : 0, as_stream(stream));
+    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, nullptr, nullptr, pos, nullptr, 1, 1, 0, pos + 1,
+                            pos + 1, nh, nkv, hs, h0, h1, half ? 1 : 0, as_stream(stream));
   });
 }
 
@@ -162,8 +162,8 @@ int b200k_attention_batch(float *out, const float *q, const void *kc, const void
   return guarded([&] {
     if (!seq || !pos || n < 0 || nh < 1 || nkv < 1 || nh % nkv || scratch_positions < 1)
       return fail(B200FWD_EINVAL, "attention_batch: bad arguments");
-    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, seq, pos, 0, n, seq_stride, scratch_positions,
-                            scratch_positions, nh, nkv, hs, 0, nh, half ? 1 : 0, as_stream(stream));
+    return launch_attention(out, nh * hs, q, nh * hs, kc, vc, att, seq, pos, 0, nullptr, n, n, seq_stride,
+                            scratch_positions, scratch_positions, nh, nkv, hs, 0, nh, half ? 1 : 0, as_stream(stream));
   });
 }
 

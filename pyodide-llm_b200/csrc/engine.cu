@@ -98,7 +98,7 @@ struct b200fwd_engine {
   float *xl = nullptr, *picked = nullptr, *logits = nullptr;
   int logit_rows = 0;
   int32_t *argmax = nullptr;
-  int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tensor-core error
+  int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tc error, -, tiles[2T]
   CUtensorMap xmap[2], xsmap[2]; // the activations and their scales, for tiles of 16 and 32 tokens
   bool tensor_cores = true;
   int32_t *meta_h = nullptr;    // pinned host copy
@@ -118,6 +118,7 @@ struct b200fwd_engine {
   int32_t *step_d() { return meta + 4 * T; }
   int32_t *bad_d() { return meta + 4 * T + 1; }
   int32_t *tc_error_d() { return meta + 4 * T + 2; }
+  int32_t *tiles_d() { return meta + 4 * T + 4; }
   int esize() const { return half ? 2 : 4; }
   int64_t seq_stride() const { return (int64_t)layers * 2 * capacity * kvDim; }
   uint8_t *layer_keys(int l) { return cache + (int64_t)(l * 2) * capacity * kvDim * esize(); }
@@ -250,9 +251,9 @@ int alloc_activations(b200fwd_engine *e) {
   CHECK(alloc(e, (void **)&e->xl, (size_t)T * e->dim * 4));
   CHECK(alloc(e, (void **)&e->picked, (size_t)T * std::max(1, e->nch) * 4));
   CHECK(alloc(e, (void **)&e->argmax, (size_t)T * 4));
-  CHECK(alloc(e, (void **)&e->meta, (size_t)(4 * T + 4) * 4));
-  B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(4 * T + 4) * 4, e->stream));
-  B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(4 * T + 4) * 4));
+  CHECK(alloc(e, (void **)&e->meta, (size_t)(6 * T + 4) * 4));
+  B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(6 * T + 4) * 4, e->stream));
+  B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(6 * T + 4) * 4));
   // the activations' TMA maps (rows of XQ bytes, one per token) and their scales' (rows of XQ/32 floats), for tiles
   // of 16 and 32 tokens
   const int bns[2] = {16, 32};
@@ -332,8 +333,9 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
 }
 
 // the layers over n tokens whose ids, slots and positions are in meta (device); the logits of the `want` tokens
-// (their indices in want_d) into logits rows 0..want-1, and their argmax. Enqueues only (graph-capturable).
-int forward_device(b200fwd_engine *e, int n, int want, int max_count) {
+// (their indices in want_d) into logits rows 0..want-1, and their argmax. ntiles > 0: the attention's token tiles
+// are in tiles_d; 0: every token its own. Enqueues only (graph-capturable).
+int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles) {
   cudaStream_t st = e->stream;
   const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32, QKV = e->QKV;
   const int shift = e->bias;  // activations stored less the bias
@@ -347,8 +349,8 @@ int forward_device(b200fwd_engine *e, int n, int want, int max_count) {
                             e->layer_values(l), e->seq_stride(), e->half ? 1 : 0, e->heads, e->kvHeads, e->hs,
                             e->plan.rotary, st));
     CHECK(launch_attention(e->xb, QD, q, QKV, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(), 0,
-                           n, e->seq_stride(), e->capacity, max_count, e->heads, e->kvHeads, e->hs, 0, e->heads,
-                           e->half ? 1 : 0, st));
+                           ntiles ? e->tiles_d() : nullptr, ntiles, n, e->seq_stride(), e->capacity, max_count,
+                           e->heads, e->kvHeads, e->hs, 0, e->heads, e->half ? 1 : 0, st));
     CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, XS, st, shift));
     CHECK(matmul(e, e->wo, l, e->x, D, 1, n));
     CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
@@ -411,8 +413,20 @@ int run(b200fwd_engine *e, int n, const int32_t *slots, const int32_t *tokens, c
   }
   for (int i = 0, w = 0; i < n; i++)
     if (want && want[i]) m[3 * T + w++] = i;
+  // the attention's tiles: runs of up to ATTN_TILE tokens of one slot at consecutive positions
+  int ntiles = 0;
+  for (int i = 0; i < n;) {
+    int j = i + 1;
+    const int si = slots ? slots[i] : 0;
+    while (j < n && j - i < ATTN_TILE && (slots ? slots[j] : 0) == si && pos[j] == pos[j - 1] + 1) j++;
+    m[4 * T + 4 + 2 * ntiles] = i;
+    m[4 * T + 4 + 2 * ntiles + 1] = j - i;
+    ntiles++;
+    i = j;
+  }
   B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T) * 4, cudaMemcpyHostToDevice, e->stream));
-  CHECK(forward_device(e, n, W, maxpos + 1));
+  B200_CUDA(cudaMemcpyAsync(e->tiles_d(), m + 4 * T + 4, (size_t)(2 * ntiles) * 4, cudaMemcpyHostToDevice, e->stream));
+  CHECK(forward_device(e, n, W, maxpos + 1, ntiles));
   if (W) {
     if (logits_out)
       B200_CUDA(cudaMemcpyAsync(logits_out, e->logits, (size_t)W * e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
@@ -746,7 +760,7 @@ int b200fwd_generate_greedy(b200fwd_engine *e, int32_t n, const int32_t *slots, 
     cudaGraphExec_t exec = nullptr;
     const uint64_t before = launches.load();
     B200_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = forward_device(e, n, n, e->capacity);
+    int rc = forward_device(e, n, n, e->capacity, 0);
     if (!rc)
       rc = launch_advance(e->tokens_d(), e->pos_d(), e->argmax, e->history, steps, e->step_d(), n, e->logits, e->vocab,
                           e->bad_d(), e->stream);

@@ -16,7 +16,6 @@ namespace {
 
 constexpr unsigned FULL = 0xffffffffu;
 constexpr int MV_WARPS = 8;
-constexpr size_t MAX_SOFTMAX_SMEM = 200 * 1024;
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
@@ -331,143 +330,6 @@ __global__ void rope_cache_kernel(float *q, int64_t q_stride, const float *k, co
   }
 }
 
-template <bool HALF>
-__device__ __forceinline__ float kv_at(const void *base, int64_t i) {
-  if (HALF) return half_to_float(reinterpret_cast<const uint16_t *>(base)[i]);
-  return reinterpret_cast<const float *>(base)[i];
-}
-
-// kernel.ts:462-498 the scores of one block of ATTN_CHUNK positions, every query head of one kv head: a thread a
-// position, four lane accumulators per head over the fours of the head, summed (l0+l2)+(l1+l3), the rest after;
-// times 1/sqrt(hs).
-template <bool HALF>
-__global__ void attn_scores_kernel(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
-                                   const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs,
-                                   int h0, int h1) {
-  extern __shared__ float smem[];
-  const int tok = blockIdx.z, kvh = blockIdx.y, chunk = blockIdx.x;
-  const int count = (pos ? pos[tok] : pos0) + 1;
-  const int t0 = chunk * ATTN_CHUNK;
-  if (t0 >= count) return;
-  const int G = nh / nkv, kvDim = nkv * hs, hs4 = hs & ~3;
-  const int64_t sbase = (int64_t)(seq ? seq[tok] : 0) * seq_stride;
-  float *qs = smem;  // [G][hs]
-  for (int i = threadIdx.x; i < G * hs; i += blockDim.x) qs[i] = q[(int64_t)tok * q_stride + kvh * G * hs + i];
-  __syncthreads();
-  const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
-  const int t = t0 + threadIdx.x;
-  const bool valid = t < count;
-  const int64_t krow = sbase + (int64_t)t * kvDim + (int64_t)kvh * hs;
-  for (int g = 0; g < G; g++) {
-    const int h = kvh * G + g;
-    const bool want = valid && h >= h0 && h < h1;
-    if (want) {
-      const float *qh = qs + g * hs;
-      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-      int j = 0;
-      for (; j < hs4; j += 4) {
-        a0 = fadd(a0, fmul(qh[j], kv_at<HALF>(kc, krow + j)));
-        a1 = fadd(a1, fmul(qh[j + 1], kv_at<HALF>(kc, krow + j + 1)));
-        a2 = fadd(a2, fmul(qh[j + 2], kv_at<HALF>(kc, krow + j + 2)));
-        a3 = fadd(a3, fmul(qh[j + 3], kv_at<HALF>(kc, krow + j + 3)));
-      }
-      float s = fadd(fadd(a0, a2), fadd(a1, a3));
-      for (; j < hs; j++) s = fadd(s, fmul(qh[j], kv_at<HALF>(kc, krow + j)));
-      att[((int64_t)tok * nh + h) * P + t] = fmul(s, isq);
-    }
-  }
-}
-
-// kernel.ts:499-521 softmax of one head: the largest, exp of every score less it (vexp on the fours, fexp after),
-// the sum in four lane chains ((0+1)+2)+3 then the rest one by one, and every weight times 1/sum
-__global__ void attn_softmax_kernel(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1) {
-  extern __shared__ float e[];
-  __shared__ float part[5];
-  __shared__ float wm[32];
-  const int tok = blockIdx.y, h = blockIdx.x;
-  if (h < h0 || h >= h1) return;
-  const int count = (pos ? pos[tok] : pos0) + 1, count4 = count & ~3;
-  float *row = att + ((int64_t)tok * nh + h) * P;
-  // the largest from -FLT_MAX, a NaN kept (kernel.ts:423-445: the order does not matter)
-  float mx = -FLT_MAX;
-  for (int t = threadIdx.x; t < count; t += blockDim.x) mx = wmax(mx, row[t]);
-  for (int o = 16; o > 0; o >>= 1) mx = wmax(mx, __shfl_xor_sync(FULL, mx, o));
-  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = -FLT_MAX;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = wmax(mx, wm[w]);
-  for (int t = threadIdx.x; t < count; t += blockDim.x) {
-    const float d = fsub(row[t], mx);
-    e[t] = t < count4 ? vexp(d) : fexp(d);
-  }
-  __syncthreads();
-  if (threadIdx.x < 4) {
-    float acc = 0.0f;
-    for (int t = threadIdx.x; t < count4; t += 4) acc = fadd(acc, e[t]);
-    part[threadIdx.x] = acc;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float sum = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
-    for (int t = count4; t < count; t++) sum = fadd(sum, e[t]);
-    part[4] = fdiv(1.0f, sum);
-  }
-  __syncthreads();
-  const float inv = part[4];
-  for (int t = threadIdx.x; t < count; t += blockDim.x) row[t] = fmul(e[t], inv);
-}
-
-// kernel.ts:522-565 the weighted sum of the values: per output, positions in fours ((w0 v0 + w1 v1) + (w2 v2 +
-// w3 v3)) added in order (a value past the fours of the head: the adds one after another), then the positions
-// past the fours one at a time. A thread takes two neighbouring values of one head.
-template <bool HALF>
-__global__ void attn_values_kernel(float *out, int64_t out_stride, const void *vc, const float *att,
-                                   const int32_t *seq, const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh,
-                                   int nkv, int hs, int h0, int h1) {
-  const int tok = blockIdx.y, kvh = blockIdx.x;
-  const int G = nh / nkv, hp = (hs + 1) / 2, kvDim = nkv * hs, hs4 = hs & ~3;
-  const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
-  if (g >= G) return;
-  const int h = kvh * G + g;
-  if (h < h0 || h >= h1) return;
-  const int count = (pos ? pos[tok] : pos0) + 1, count4 = count & ~3;
-  const int64_t sbase = (int64_t)(seq ? seq[tok] : 0) * seq_stride + (int64_t)kvh * hs;
-  const float *w = att + ((int64_t)tok * nh + h) * P;
-  const int j0 = 2 * jp, j1 = j0 + 1;
-  const bool has1 = j1 < hs;
-  float o0 = 0.0f, o1 = 0.0f;
-  int t = 0;
-  for (; t < count4; t += 4) {
-    const float4 wt = make_float4(w[t], w[t + 1], w[t + 2], w[t + 3]);
-    const int64_t r0 = sbase + (int64_t)t * kvDim;
-    const float v00 = kv_at<HALF>(vc, r0 + j0), v10 = kv_at<HALF>(vc, r0 + kvDim + j0);
-    const float v20 = kv_at<HALF>(vc, r0 + 2 * kvDim + j0), v30 = kv_at<HALF>(vc, r0 + 3 * kvDim + j0);
-    if (j0 < hs4) {
-      o0 = fadd(o0, fadd(fadd(fmul(wt.x, v00), fmul(wt.y, v10)), fadd(fmul(wt.z, v20), fmul(wt.w, v30))));
-    } else {
-      o0 = fadd(fadd(fadd(fadd(o0, fmul(wt.x, v00)), fmul(wt.y, v10)), fmul(wt.z, v20)), fmul(wt.w, v30));
-    }
-    if (has1) {
-      const float v01 = kv_at<HALF>(vc, r0 + j1), v11 = kv_at<HALF>(vc, r0 + kvDim + j1);
-      const float v21 = kv_at<HALF>(vc, r0 + 2 * kvDim + j1), v31 = kv_at<HALF>(vc, r0 + 3 * kvDim + j1);
-      if (j1 < hs4) {
-        o1 = fadd(o1, fadd(fadd(fmul(wt.x, v01), fmul(wt.y, v11)), fadd(fmul(wt.z, v21), fmul(wt.w, v31))));
-      } else {
-        o1 = fadd(fadd(fadd(fadd(o1, fmul(wt.x, v01)), fmul(wt.y, v11)), fmul(wt.z, v21)), fmul(wt.w, v31));
-      }
-    }
-  }
-  for (; t < count; t++) {
-    const float wt = w[t];
-    const int64_t r0 = sbase + (int64_t)t * kvDim;
-    o0 = fadd(o0, fmul(wt, kv_at<HALF>(vc, r0 + j0)));
-    if (has1) o1 = fadd(o1, fmul(wt, kv_at<HALF>(vc, r0 + j1)));
-  }
-  float *o = out + (int64_t)tok * out_stride + h * hs;
-  o[j0] = o0;
-  if (has1) o[j1] = o1;
-}
-
 __global__ void add_columns_kernel(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride,
                                    int nc, int n, int count) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -671,50 +533,6 @@ int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v
                                               reinterpret_cast<uint8_t *>(kc), reinterpret_cast<uint8_t *>(vc),
                                               seq_stride, half, nh, nkv, hs, rot);
   B200_LAUNCHED("rope_cache_kernel");
-  return 0;
-}
-
-int prepare_attention() {
-  int device = 0;
-  B200_CUDA(cudaGetDevice(&device));
-  static std::atomic<uint64_t> opted{0};
-  if (device >= 64 || !(opted.load() & (1ull << device))) {
-    B200_CUDA(cudaFuncSetAttribute(attn_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_SOFTMAX_SMEM));
-    if (device < 64) opted.fetch_or(1ull << device);
-  }
-  return 0;
-}
-
-int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
-                     float *att, const int32_t *seq, const int32_t *pos, int pos0, int count, int64_t seq_stride,
-                     int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int half, cudaStream_t stream) {
-  if (count <= 0) return 0;
-  if (nkv <= 0 || nh % nkv) return fail(B200FWD_EINVAL, "attention: heads must be a multiple of the kv heads");
-  if (max_count > P) return fail(B200FWD_EINVAL, "attention: a position past the scratch");
-  const int G = nh / nkv;
-  const int chunks = (max_count + ATTN_CHUNK - 1) / ATTN_CHUNK;
-  const size_t smem_scores = (size_t)(G * hs) * sizeof(float);
-  dim3 g1(chunks, nkv, count);
-  if (half)
-    attn_scores_kernel<true><<<g1, ATTN_CHUNK, smem_scores, stream>>>(q, q_stride, kc, att, seq, pos, pos0,
-                                                                       seq_stride, P, nh, nkv, hs, h0, h1);
-  else
-    attn_scores_kernel<false><<<g1, ATTN_CHUNK, smem_scores, stream>>>(q, q_stride, kc, att, seq, pos, pos0,
-                                                                        seq_stride, P, nh, nkv, hs, h0, h1);
-  B200_LAUNCHED("attn_scores_kernel");
-  const size_t smem_soft = (size_t)max_count * sizeof(float);
-  if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
-  CHECK_RC(prepare_attention());
-  attn_softmax_kernel<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
-  B200_LAUNCHED("attn_softmax_kernel");
-  const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
-  if (half)
-    attn_values_kernel<true><<<dim3(nkv, count), threads, 0, stream>>>(out, out_stride, vc, att, seq, pos, pos0,
-                                                                        seq_stride, P, nh, nkv, hs, h0, h1);
-  else
-    attn_values_kernel<false><<<dim3(nkv, count), threads, 0, stream>>>(out, out_stride, vc, att, seq, pos, pos0,
-                                                                         seq_stride, P, nh, nkv, hs, h0, h1);
-  B200_LAUNCHED("attn_values_kernel");
   return 0;
 }
 

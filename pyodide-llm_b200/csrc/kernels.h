@@ -55,13 +55,16 @@ int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *to
 int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v, int64_t kv_stride, const float *cos,
                       const float *sin, const int32_t *pos, const int32_t *seq, int count, void *kc, void *vc,
                       int64_t seq_stride, int half, int nh, int nkv, int hs, int rot, cudaStream_t stream);
-// kernel.ts:447-566 attentionOf for count tokens, each against its sequence's cache up to its position (device
-// arrays seq and pos; or, with pos null, every token at pos0 of sequence 0). att: [count][nh][P] scratch
-// (P >= max position + 1), left holding the softmax weights; max_count bounds pos + 1 for the grid. Heads h0..h1.
+// kernel.ts:447-566 attentionOf for count tokens (attention.cu), each against its sequence's cache up to its
+// position: device arrays seq and pos, or, with pos null, every token at pos0 of sequence 0. tiles: ntiles pairs
+// (first token, count) of up to 16 consecutive tokens of one sequence at consecutive positions, sharing the keys and
+// values they read; null: every token its own tile. att: [count][nh][P] scratch (P >= max position + 1), left
+// holding the softmax weights; max_count bounds pos + 1 for the grid. Heads h0..h1.
 int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
-                     float *att, const int32_t *seq, const int32_t *pos, int pos0, int count, int64_t seq_stride,
-                     int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int half, cudaStream_t stream);
-constexpr int ATTN_CHUNK = 128;
+                     float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
+                     int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1,
+                     int half, cudaStream_t stream);
+constexpr int ATTN_TILE = 16;  // tokens of a tile at most
 // the attention kernels' shared-memory opt-in on the current device (once; before any graph capture)
 int prepare_attention();
 // kernel.ts:671-689 add_columns for count tokens (y rows y_stride apart, a rows a_stride apart)

@@ -190,6 +190,15 @@ int b200k_rope(float *v, const float *fcr, const float *fci, int32_t nh, int32_t
  * (device), which ends up holding the softmax weights as the reference's does. */
 int b200k_attention(float *out, const float *q, const void *kc, const void *vc, float *att, int32_t pos, int32_t nh,
                     int32_t nkv, int32_t hs, int32_t h0, int32_t h1, int32_t half, b200fwd_stream stream);
+/* No counterpart in the reference. b200k_attention for callers that cannot allocate device memory where they call
+ * (inside a stream capture, where cudaMalloc is not allowed; on a latency path that must not stall the device the
+ * way cudaMalloc can; under a fixed device budget): the same numbers, with the softmax scratch in a 4 MiB array of
+ * the library's own, which every GPU that loads the library holds until exit. nh * (pos + 1) may be at most
+ * 1048576 (else B200FWD_EINVAL). The first call on a device looks the array up, so make it before any capture.
+ * Every call shares the array: calls that overlap on the GPU race. Nothing needs zeroing; it keeps the last
+ * call's softmax weights. */
+int b200k_attention_static(float *out, const float *q, const void *kc, const void *vc, int32_t pos, int32_t nh,
+                           int32_t nkv, int32_t hs, int32_t h0, int32_t h1, int32_t half, b200fwd_stream stream);
 /* kernel.ts:570-599 to_f16 (round to nearest even, NumPy's astype(float16)) and kernel.ts:604-608 from_f16. */
 int b200k_to_f16(uint16_t *out, const float *x, int64_t n, b200fwd_stream stream);
 int b200k_from_f16(float *out, const uint16_t *x, int64_t n, b200fwd_stream stream);

@@ -148,6 +148,7 @@ def load():
         "b200k_rmsnorm": (P, P, P, I32, ctypes.c_float, I32, I64, P),
         "b200k_rope": (P, P, P, I32, I32, I32, P),
         "b200k_attention": (P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, P),
+        "b200k_attention_static": (P, P, P, P, I32, I32, I32, I32, I32, I32, I32, P),
         "b200k_to_f16": (P, P, I64, P),
         "b200k_from_f16": (P, P, I64, P),
         "b200k_swiglu": (P, P, P, I64, P),

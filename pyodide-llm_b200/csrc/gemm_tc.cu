@@ -4,14 +4,14 @@
 // The reference's number for (row r, token t) is a float chain over the row's groups of 32: each group's exact
 // integer dot(w, q - 64) times (weight scale x activation scale), rounded once, added into lane g % 4 for the groups
 // below the last four, the lanes added ((0 + 1) + 2) + 3, then the groups past the fours one at a time. Here:
-//   - TMA brings 128 weight rows x 128 bytes (four groups) and BN tokens' activations x 128 bytes per stage into
-//     shared memory (128-byte swizzle; no multicast);
-//   - one thread issues one tcgen05.mma kind::i8 per group (K = 32: exactly one group) into a TMEM slot of its own
-//     (128 lanes = rows, BN columns = tokens): every group's int32 sums, exact, none added to another;
-//   - 16 epilogue warps, four per TMEM lane quarter, one per chain lane k = g % 4, read their groups' sums
-//     (tcgen05.ld) and run the reference's chain for every token of their rows with paired float32 operations
-//     (add/mul .rn .f32x2: each element rounded on its own, as f32x4 in WASM); then the four lanes meet in shared
-//     memory, are added in order, and the lane-0 warps add the groups past the fours.
+//   - warp 0: TMA brings 128 weight rows x 128 bytes (four groups), BN tokens' activations x 128 bytes and both
+//     scale tiles per stage into shared memory, 8 stages deep (128-byte swizzle; no multicast);
+//   - warp 1: one thread issues one tcgen05.mma kind::i8 per group (K = 32: exactly one group) into a TMEM column
+//     block of its own (128 lanes = rows, BN columns = tokens): every group's int32 sums, exact, none added to
+//     another. TMEM holds several stages at once (slots), and one tcgen05.commit per stage releases a slot;
+//   - warps 2..17 (epilogue): four per TMEM lane quarter, each with BN / 4 tokens, read their groups' sums
+//     (tcgen05.ld) and keep the reference's four chain accumulators of each (row, token) in registers, with one
+//     rounding per float operation (__fmul_rn / __fadd_rn; no contraction, built with --fmad=false).
 // Every mbarrier wait has an iteration limit: past it the kernel records an error and returns (no hang).
 #include <cuda.h>
 #include <cudaTypedefs.h>

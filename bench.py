@@ -178,61 +178,20 @@ def reference_arm(args):
     return 0
 
 
-def matmul_roofline(lib, M, stream, peaks, reps=12):
-    """The int8 matmul alone at the decode step's shapes, as the engine runs them (q|k|v fused, o, w1|w3 fused, w2)
-    at M tokens through b200k_matmul_q8s (the tensor cores from 16 tokens on), cycling over 8 distinct layers'
-    worth of weights (2 GB, beyond L2). CUDA events on the stream."""
-    import torch
-
-    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
-    layers = 8
-    g = torch.Generator(device="cuda")
-    g.manual_seed(1)
-    mats = []
-    for rows, n in shapes:
-        w = torch.randint(-127, 128, (layers, rows, n), dtype=torch.int8, device="cuda", generator=g)
-        s = torch.rand((layers, rows, n // 32), device="cuda", generator=g) * 0.019 + 0.001
-        mats.append((w, s, rows, n))
-    nmax = 14336
-    xq = torch.randint(-63, 64, (M, nmax), dtype=torch.int8, device="cuda", generator=g)
-    xs = torch.rand((M, nmax // 32), device="cuda", generator=g) * 0.1
-    out = torch.empty((M, 28672), device="cuda")
-    st = torch.cuda.ExternalStream(stream)
-    import ctypes
-
-    def launch(i):
-        w, s, rows, n = mats[i % len(mats)]
-        layer = (i // len(mats)) % layers
-        rc = lib.b200k_matmul_q8s(ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(xq.data_ptr()),
-                                  ctypes.c_void_p(xs.data_ptr()), ctypes.c_void_p(w[layer].data_ptr()),
-                                  ctypes.c_void_p(s[layer].data_ptr()), n // 32, n, rows, M, 28672, nmax,
-                                  nmax // 32, ctypes.c_void_p(stream))
-        assert rc == 0
-        return rows * n * (1 + 4 / 32) + M * n * (1 + 4 / 32) + M * rows * 4
-
-    for i in range(len(mats) * 2):
-        launch(i)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    count = len(mats) * reps
-    total = 0.0
-    start.record(st)
-    for i in range(count):
-        total += launch(i)
-    end.record(st)
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    per_launch_bytes = total / count
-    per_launch_s = ms / 1e3 / count
+def matmul_roofline(eng, M, peaks, reps=3):
+    """The int8 matmul (the dominant kernel) alone, as the engine launches it at the decode step's M tokens: every
+    layer's q|k|v, o, w1|w3 and w2, then the classifier (8.9 GB of weights, far beyond L2), back to back on the
+    engine's stream, timed with CUDA events (b200fwd_time_matmuls), right after the timed steps on the same engine."""
+    ms, nbytes, launches = eng.time_matmuls(M, reps)
+    per_launch_s = ms / 1e3 / launches
+    per_launch_bytes = nbytes / launches
     achieved = per_launch_bytes / per_launch_s / 1e9
     peak = float(peaks["hbm_gbs"])
-    del mats
-    torch.cuda.empty_cache()
     return {"kernel": "q8_gemm_tc (int8 group-32 matmul, tcgen05, exact order)" if M >= 16 else
             "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": None, "M": M, "per_launch_us": per_launch_s * 1e6,
-            "algorithmic_bytes_per_launch": per_launch_bytes}
+            "traffic": None, "M": M, "per_launch_us": per_launch_s * 1e6, "launches_per_pass": launches,
+            "algorithmic_bytes_per_launch": per_launch_bytes, "pass_ms": ms}
 
 
 def b200_arm(args):
@@ -270,6 +229,7 @@ def b200_arm(args):
 
     def step(events=None):
         """one batch: prefill positions 0..P-2 in blocks, then G greedy steps from the last prompt token"""
+        torch.cuda.nvtx.range_push("prefill")
         for b0 in range(0, P - 1, args.block):
             n = min(args.block, P - 1 - b0)
             sl = np.repeat(slots_all, n)
@@ -282,10 +242,13 @@ def b200_arm(args):
             if events is not None:
                 events.append(torch.cuda.Event(enable_timing=True))
                 events[-1].record(st)
+        torch.cuda.nvtx.range_pop()
         if events is not None:
             events.append(torch.cuda.Event(enable_timing=True))
             events[-1].record(st)
+        torch.cuda.nvtx.range_push("decode")
         ids = eng.generate_greedy(slots_all, prompts[:, P - 1], np.full(S, P - 1, np.int32), G)
+        torch.cuda.nvtx.range_pop()
         if events is not None:
             events.append(torch.cuda.Event(enable_timing=True))
             events[-1].record(st)
@@ -333,7 +296,7 @@ def b200_arm(args):
     result = None
     if rank == 0:
         peaks, which = measured_peaks()
-        roof = matmul_roofline(abi.load(), S, stream, peaks)
+        roof = matmul_roofline(eng, S, peaks)
         roof["peak_source"] = which
         cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
         del ckpt_host

@@ -148,6 +148,13 @@ int b200fwd_reset_slot(b200fwd_engine *engine, int32_t slot);
 int b200fwd_stream_of(b200fwd_engine *engine, b200fwd_stream *out);
 /* The number of kernels the engine launched since it was made (counted on the host at every launch). */
 int b200fwd_launch_count(b200fwd_engine *engine, uint64_t *out);
+/* No counterpart in the reference: a measurement aid. One pass = the int8 matmul of every weight matrix at `count`
+ * tokens, as the forward pass launches it (each layer's q|k|v, o, w1|w3, w2, then the classifier), on the engine's
+ * current activations, into a buffer of its own (the engine's state is left as it was). Runs one
+ * warm-up pass and `reps` timed ones back to back; gives the GPU time of one pass (CUDA events on the engine's
+ * stream), its algorithmic bytes (weights + scales + activations read once, outputs written once) and its launches. */
+int b200fwd_time_matmuls(b200fwd_engine *engine, int32_t count, int32_t reps, float *ms_per_pass,
+                         double *bytes_per_pass, int32_t *launches_per_pass);
 
 /* ---------------------------------------------------------------------------------------------- the kernels
  * Device pointers, a stream, and the reference's arguments. `count` tokens of a prompt (T108) sit `*_stride`
@@ -169,9 +176,9 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream);
 /* kernel_relaxed.ts:34-67 / 164-183 on activations already less the bias (xq[i] = q[i] - 64, signed; the engine
  * keeps them so): all `rows` rows of W for `count` tokens, the same numbers to the bit. From 16 tokens on (with
- * n >= 128, rows >= 128, and ws_stride, s_stride multiples of 4 floats: TMA rows of whole 16 bytes) it runs on the
- * tensor cores (tcgen05.mma kind::i8, one MMA per group of 32), else on the CUDA cores. ws: row r's scales at
- * ws + r * ws_stride (0: n / 32). xq, wq, ws, xs 16-byte aligned; q_stride a multiple of 16. */
+ * n >= 128, rows >= 128, and ws_stride a multiple of 4 floats: TMA rows of whole 16 bytes) it runs on the tensor
+ * cores (tcgen05.mma kind::i8, one MMA per group of 32), else on the CUDA cores. ws: row r's scales at
+ * ws + r * ws_stride (0: n / 32). xq, wq, ws 16-byte aligned; q_stride a multiple of 16. */
 int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
                      int64_t ws_stride, int32_t n, int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride,
                      int64_t s_stride, b200fwd_stream stream);

@@ -144,6 +144,13 @@ class Engine:
         abi.check(self._lib.b200fwd_launch_count(self._h, ctypes.byref(out)), "launch_count")
         return out.value
 
+    def time_matmuls(self, count, reps=3):
+        """(ms, bytes, launches) of one pass of every matmul at `count` tokens (b200fwd_time_matmuls)."""
+        ms, nbytes, launches = ctypes.c_float(), ctypes.c_double(), ctypes.c_int32()
+        abi.check(self._lib.b200fwd_time_matmuls(self._h, count, reps, ctypes.byref(ms), ctypes.byref(nbytes),
+                                                 ctypes.byref(launches)), "time_matmuls")
+        return ms.value, nbytes.value, launches.value
+
     def stream(self):
         out = ctypes.c_void_p()
         abi.check(self._lib.b200fwd_stream_of(self._h, ctypes.byref(out)), "stream")

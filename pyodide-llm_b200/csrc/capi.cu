@@ -40,7 +40,7 @@ int matmul(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, con
   jobs.njobs = 1;
   jobs.n = n;
   jobs.total_rows = r1 - r0;
-  return launch_matvec(jobs, xq, xs, q_stride, s_stride, count, relaxed, as_stream(stream));
+  return launch_matvec(jobs, xq, xs, q_stride, s_stride, 1, count, relaxed, as_stream(stream));
 }
 
 }  // namespace
@@ -51,7 +51,7 @@ int b200k_quantize_x(int8_t *xq, float *xs, const float *x, int32_t n, int32_t b
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream) {
   return guarded([&] {
     if (bias != 0 && bias != 64) return fail(B200FWD_EINVAL, "quantize_x: bias must be 0 or 64");
-    return launch_quantize(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride, as_stream(stream));
+    return launch_quantize(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride, 1, as_stream(stream));
   });
 }
 
@@ -80,26 +80,35 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     if (ws_stride < n / 32) return fail(B200FWD_EINVAL, "matmul_q8s: ws_stride below n / 32");
     cudaStream_t st = as_stream(stream);
     // the tensor cores need whole TMA boxes and scale rows of whole 16 bytes: else the CUDA cores
-    if (count < 16 || n < 128 || rows < 128 || ws_stride % 4 || s_stride % 4 ||
-        (reinterpret_cast<uintptr_t>(ws) % 16) || (reinterpret_cast<uintptr_t>(xs) % 16)) {
+    if (count < 16 || n < 128 || rows < 128 || ws_stride % 4 || (reinterpret_cast<uintptr_t>(ws) % 16)) {
       MatJobs jobs{};
       jobs.job[0] = {wq, ws, nullptr, xout, rows, 0, out_stride, (int)ws_stride};
       jobs.njobs = 1;
       jobs.n = n;
       jobs.total_rows = rows;
       jobs.signed_input = 1;
-      return launch_matvec(jobs, xq, xs, q_stride, s_stride, count, true, st);
+      return launch_matvec(jobs, xq, xs, q_stride, s_stride, 1, count, true, st);
     }
     int *err = nullptr;
     B200_CUDA(cudaGetSymbolAddress((void **)&err, capi_tc_error));
     const int row_tiles = (rows + 127) / 128;
     int bn = 32;
     while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
+    // the kernel reads the activation scales one row per group: a stream-ordered copy in that layout
+    const int64_t tstride = (count + 3) / 4 * 4;
+    float *xs_g = nullptr;
+    B200_CUDA(cudaMallocAsync((void **)&xs_g, (size_t)tstride * (n / 32) * 4, st));
+    struct Free {
+      float *p;
+      cudaStream_t s;
+      ~Free() { cudaFreeAsync(p, s); }
+    } free_xs{xs_g, st};
+    int rc = launch_scales_by_group(xs_g, tstride, xs, s_stride, count, n / 32, st);
     GemmMaps maps;
-    int rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
+    if (!rc) rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
     if (!rc) rc = make_i8_map(&maps.x, xq, n, count, q_stride, bn);
     if (!rc) rc = make_scale_map(&maps.ws, ws, ws_stride, rows, ws_stride, 128);
-    if (!rc) rc = make_scale_map(&maps.xs, xs, n / 32, count, s_stride, bn);
+    if (!rc) rc = make_token_scale_map(&maps.xs, xs_g, count, n / 32, tstride, bn);
     if (rc) return rc;
     GemmArgs a{};
     a.out = xout;

@@ -90,6 +90,7 @@ struct b200fwd_engine {
   uint8_t *cache = nullptr;
   // activations
   int T = 0;
+  int TP = 0;  // T rounded up to 32: the activation scales are [XQ/32 groups][TP tokens]
   int QKV = 0;
   float *x = nullptr, *xb = nullptr, *qkv = nullptr, *h13 = nullptr;
   float *att = nullptr;
@@ -247,21 +248,21 @@ int alloc_activations(b200fwd_engine *e) {
   CHECK(alloc(e, (void **)&e->qkv, (size_t)T * e->QKV * 4));
   CHECK(alloc(e, (void **)&e->h13, (size_t)T * 2 * e->hidden * 4));
   CHECK(alloc(e, (void **)&e->xq, (size_t)T * e->XQ));
-  CHECK(alloc(e, (void **)&e->xs, (size_t)T * (e->XQ / 32) * 4));
+  CHECK(alloc(e, (void **)&e->xs, (size_t)e->TP * (e->XQ / 32) * 4));
   CHECK(alloc(e, (void **)&e->xl, (size_t)T * e->dim * 4));
   CHECK(alloc(e, (void **)&e->picked, (size_t)T * std::max(1, e->nch) * 4));
   CHECK(alloc(e, (void **)&e->argmax, (size_t)T * 4));
   CHECK(alloc(e, (void **)&e->meta, (size_t)(6 * T + 4) * 4));
   B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(6 * T + 4) * 4, e->stream));
   B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(6 * T + 4) * 4));
-  // the activations' TMA maps (rows of XQ bytes, one per token) and their scales' (rows of XQ/32 floats), for tiles
-  // of 16 and 32 tokens
+  // the activations' TMA maps (rows of XQ bytes, one per token) and their scales' (rows of TP floats, one per group),
+  // for tiles of 16 and 32 tokens
   const int bns[2] = {16, 32};
   e->tensor_cores = e->tensor_cores && T >= 32 && e->XQ >= 128;
   if (e->tensor_cores)
     for (int i = 0; i < 2; i++) {
       CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
-      CHECK(make_scale_map(&e->xsmap[i], e->xs, e->XQ / 32, T, e->XQ / 32, bns[i]));
+      CHECK(make_token_scale_map(&e->xsmap[i], e->xs, T, e->XQ / 32, e->TP, bns[i]));
     }
   return 0;
 }
@@ -303,7 +304,6 @@ int grow(b200fwd_engine *e, int pos) {
 // one matrix of one layer times the quantized activations of count tokens (in e->xq, less the bias): the tensor
 // cores from 16 tokens on (gemm_tc.cu), the CUDA cores below (kernels.cu); the same numbers either way
 int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t out_stride, int accumulate, int count) {
-  const int XS = e->XQ / 32;
   // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 32 tokens: never past the tensors' extents)
   if (count >= 16 && e->relaxed && e->tensor_cores && m.mapped) {
     GemmArgs a{};
@@ -329,7 +329,7 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
   jobs.n = m.n;
   jobs.total_rows = m.rows;
   jobs.signed_input = 1;
-  return launch_matvec(jobs, e->xq, e->xs, e->XQ, XS, count, e->relaxed, e->stream);
+  return launch_matvec(jobs, e->xq, e->xs, e->XQ, 1, e->TP, count, e->relaxed, e->stream);
 }
 
 // the layers over n tokens whose ids, slots and positions are in meta (device); the logits of the `want` tokens
@@ -337,12 +337,12 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
 // are in tiles_d; 0: every token its own. Enqueues only (graph-capturable).
 int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles) {
   cudaStream_t st = e->stream;
-  const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, XS = e->XQ / 32, QKV = e->QKV;
+  const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, TP = e->TP, QKV = e->QKV;
   const int shift = e->bias;  // activations stored less the bias
   float *q = e->qkv, *k = e->qkv + QD, *v = e->qkv + QD + KVD;
   CHECK(launch_embed(e->emb.w, e->emb.s, e->emb.sstride, e->tokens_d(), n, D, e->x, D, st));
   for (int l = 0; l < e->layers; l++) {
-    CHECK(launch_norm_quantize(e->x, D, e->attW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
+    CHECK(launch_norm_quantize(e->x, D, e->attW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, 1, TP,
                                nullptr, 0, nullptr, nullptr, 0, st, shift));
     CHECK(matmul(e, e->wqkv, l, e->qkv, QKV, 0, n));
     CHECK(launch_rope_cache(q, QKV, k, v, QKV, e->cosT, e->sinT, e->pos_d(), e->seq_d(), n, e->layer_keys(l),
@@ -351,18 +351,18 @@ int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles
     CHECK(launch_attention(e->xb, QD, q, QKV, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(), 0,
                            ntiles ? e->tiles_d() : nullptr, ntiles, n, e->seq_stride(), e->capacity, max_count,
                            e->heads, e->kvHeads, e->hs, 0, e->heads, e->half ? 1 : 0, st));
-    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, XS, st, shift));
+    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, 1, TP, st, shift));
     CHECK(matmul(e, e->wo, l, e->x, D, 1, n));
-    CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, XS,
+    CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, 1, TP,
                                nullptr, 0, nullptr, nullptr, 0, st, shift));
     CHECK(matmul(e, e->w13, l, e->h13, 2 * HID, 0, n));
-    CHECK(launch_swiglu_quantize(e->h13, e->h13 + HID, 2 * HID, HID, e->bias, n, e->xq, XQ, e->xs, XS, st, shift));
+    CHECK(launch_swiglu_quantize(e->h13, e->h13 + HID, 2 * HID, HID, e->bias, n, e->xq, XQ, e->xs, 1, TP, st, shift));
     CHECK(matmul(e, e->w2, l, e->x, D, 1, n));
   }
   if (want <= 0) return 0;
   // forward.js:521-530: the final norm of the wanted tokens, the outlier channels apart, the classifier, the columns
   CHECK(launch_gather_rows(e->xl, D, e->x, D, e->want_d(), want, D, st));
-  CHECK(launch_norm_quantize(e->xl, D, e->finalW, D, e->eps, e->bias, want, e->xq, XQ, e->xs, XS, e->channels, e->nch,
+  CHECK(launch_norm_quantize(e->xl, D, e->finalW, D, e->eps, e->bias, want, e->xq, XQ, e->xs, 1, TP, e->channels, e->nch,
                              e->picked, nullptr, 0, st, shift));
   CHECK(matmul(e, e->wcls, 0, e->logits, e->vocab, 0, want));
   CHECK(launch_add_columns(e->logits, e->vocab, e->columns, e->picked, e->nch, e->nch, e->vocab, want, st));
@@ -473,6 +473,7 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
   e->slots = opt.slots;
   e->T = opt.max_tokens > 0 ? opt.max_tokens : std::max(512, 16 * e->slots);
   if (e->T > 65535) return fail(B200FWD_EINVAL, "max_tokens above 65535");
+  e->TP = (e->T + 31) / 32 * 32;
   e->device = opt.device;
   B200_CUDA(cudaSetDevice(e->device));
   B200_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
@@ -714,6 +715,59 @@ int b200fwd_launch_count(b200fwd_engine *e, uint64_t *out) {
   if (!e || !out) return fail(B200FWD_EINVAL, "launch_count: null argument");
   *out = launches.load() - e->launches_at_create;
   return 0;
+}
+
+int b200fwd_time_matmuls(b200fwd_engine *e, int32_t count, int32_t reps, float *ms_per_pass, double *bytes_per_pass,
+                          int32_t *launches_per_pass) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (count < 1 || count > e->T || reps < 1 || !ms_per_pass || !bytes_per_pass || !launches_per_pass)
+      return fail(B200FWD_EINVAL, "time_matmuls: bad arguments");
+    const Matrix *mats[4] = {&e->wqkv, &e->wo, &e->w13, &e->w2};
+    // every output goes to a buffer of its own, count x the most rows of any matrix
+    int most = e->wcls.rows;
+    for (const Matrix *m : mats) most = std::max(most, m->rows);
+    float *out = nullptr;
+    B200_CUDA(cudaMallocAsync((void **)&out, (size_t)count * most * 4, e->stream));
+    struct Free {
+      float *p;
+      cudaStream_t s;
+      ~Free() { cudaFreeAsync(p, s); }
+    } free_out{out, e->stream};
+    auto bytes = [&](const Matrix &m) {
+      return (double)m.rows * m.n * (1.0 + 4.0 / 32) + (double)count * m.n * (1.0 + 4.0 / 32) + 4.0 * count * m.rows;
+    };
+    double total = 0;
+    for (const Matrix *m : mats) total += e->layers * bytes(*m);
+    total += bytes(e->wcls);
+    cudaEvent_t t0, t1;
+    B200_CUDA(cudaEventCreate(&t0));
+    B200_CUDA(cudaEventCreate(&t1));
+    struct Drop {
+      cudaEvent_t a, b;
+      ~Drop() {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+      }
+    } drop{t0, t1};
+    auto pass = [&]() -> int {
+      for (int l = 0; l < e->layers; l++)
+        for (const Matrix *m : mats) CHECK(matmul(e, *m, l, out, m->rows, 0, count));
+      return matmul(e, e->wcls, 0, out, e->wcls.rows, 0, count);
+    };
+    CHECK(pass());  // warm-up
+    B200_CUDA(cudaEventRecord(t0, e->stream));
+    for (int r = 0; r < reps; r++) CHECK(pass());
+    B200_CUDA(cudaEventRecord(t1, e->stream));
+    B200_CUDA(cudaEventSynchronize(t1));
+    float ms = 0;
+    B200_CUDA(cudaEventElapsedTime(&ms, t0, t1));
+    CHECK(check_tc(e));
+    *ms_per_pass = ms / reps;
+    *bytes_per_pass = total;
+    *launches_per_pass = 4 * e->layers + 1;
+    return 0;
+  });
 }
 
 int b200fwd_generate_greedy(b200fwd_engine *e, int32_t n, const int32_t *slots, const int32_t *first,

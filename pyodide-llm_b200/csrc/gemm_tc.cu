@@ -101,10 +101,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(int bn) {
          | ((uint32_t)(BM >> 4) << 24);    // M >> 4
 }
 
+// D += A x B: TMEM holds magic_bits before a group's first and only MMA, so D = magic_bits + the group's sum
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 0, 0;\n\t"
+      "setp.eq.b32 p, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc)
       : "memory");
@@ -116,33 +117,31 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 16 consecutive TMEM columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+// Two float32 lanes at once (PTX .f32x2), each lane rounded on its own. A paired multiply whose product feeds a
+// paired add is fused into one fma below PTX (one rounding: not the reference's number); a product that is the addend
+// of an fma cannot be fused. So the chains add as fma(one, acc, product), `one` being 1.0f from a kernel argument:
+// acc * 1 is exact, and acc + product is then rounded once, as an add rounds it.
+__device__ __forceinline__ uint64_t pack2(uint32_t a, uint32_t b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
 }
-
-// two float32 lanes at once, each rounded on its own (PTX add/mul .rn .f32x2)
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
   uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
 __device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
@@ -156,7 +155,7 @@ struct Smem {
   alignas(1024) uint8_t a[STAGES][BM * KSTAGE];       // 128 weight rows x four groups
   alignas(1024) uint8_t b[STAGES][BN_MAX * KSTAGE];   // the tokens x four groups
   alignas(128) float ws[STAGES][BM][4];               // the rows' four groups' scales
-  alignas(128) float xs[STAGES][BN_MAX][4];           // the tokens' four groups' scales
+  alignas(128) float xs[STAGES][4 * BN_MAX];          // the tokens' scales: four rows (groups) of bn tokens
   uint64_t full[STAGES], empty[STAGES];
   uint64_t slot_full[8], slot_empty[8];  // TMEM stage slots: four groups' columns each
   uint32_t tmem_base;
@@ -178,9 +177,24 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
+// the same word into TPW consecutive TMEM columns of this warp's 32 lanes
+template <int TPW>
+__device__ __forceinline__ void tmem_st_same(uint32_t taddr, uint32_t v);
+template <>
+__device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_same<4>(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(v) : "memory");
+}
+
 // Warp roles: 0 TMA producer, 1 MMA issue, 2..17 epilogue. Epilogue warp w reads TMEM lane quarter w % 4 (its 32
 // rows) and token columns (w - 2) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
-// its (row, token) in registers: the chains, their sum and the groups past the fours all happen in one thread.
+// its (row, token) in registers, two tokens to a 64-bit pair: the chains, their sum and the groups past the fours
+// all happen in one thread. It also puts magic_bits back into the TMEM columns it has read, for the MMAs that reuse
+// them (D = magic_bits + the group's sum: its float is then one paired subtraction).
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
@@ -188,7 +202,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   constexpr int SLOTS = 512 / (4 * BN);  // TMEM holds this many stages' four groups at once
-  constexpr int TPW = BN / 4;
+  constexpr int TPW = BN / 4;            // tokens of an epilogue warp
+  constexpr int PAIRS = TPW / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = args.n >> 5, ng4 = ng & ~3;
   const int kstages = (args.n + KSTAGE - 1) / KSTAGE;
@@ -227,17 +242,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_2d(s.a[st], &wmap, &s.full[st], k * KSTAGE, wy);
         tma_load_2d(s.b[st], &xmap, &s.full[st], k * KSTAGE, tok0);
         tma_load_2d(s.ws[st], &wsmap, &s.full[st], k * 4, wy);
-        tma_load_2d(s.xs[st], &xsmap, &s.full[st], k * 4, tok0);
+        tma_load_2d(s.xs[st], &xsmap, &s.full[st], tok0, k * 4);
       }
     }
   } else if (warp == 1) {
     // ---- MMA issue: a stage's four groups, one MMA each (K = 32, one group) into four TMEM column blocks of the
-    // stage's slot, one commit per stage
+    // stage's slot, one commit per stage. A slot is free once every epilogue warp has read it and put magic_bits
+    // back (the first time: the epilogue's initial fill).
     const uint32_t idesc = idesc_i8(BN);
     for (int k = 0; k < kstages; k++) {
       const int st = k % STAGES, slot = k % SLOTS;
       if (!mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 2)) break;
-      if (!mbar_wait(&s.slot_empty[slot], ((k / SLOTS) & 1) ^ 1, args.error, 3)) break;
+      if (!mbar_wait(&s.slot_empty[slot], (k / SLOTS) & 1, args.error, 3)) break;
       tc_fence_after();
       if (lane == 0) {
         const int groups = min(4, ng - 4 * k);
@@ -253,19 +269,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp % 4, sub = (warp - 2) / 4;
     const uint32_t magic_bits = args.magic_bits;
     const float magic = args.magic;
+    const uint64_t magic2 = pack2(__float_as_uint(magic), __float_as_uint(magic));
+    const uint64_t one2 = pack2(__float_as_uint(args.one), __float_as_uint(args.one));
     const int rl = quarter * 32 + lane;  // the row within the tile
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
-    float acc[TPW][4];
+    // every slot's columns of this warp start as magic_bits
+#pragma unroll 1
+    for (int c = 0; c < 4 * SLOTS; c++) tmem_st_same<TPW>(taddr + (uint32_t)(c * BN), magic_bits);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int i = 0; i < SLOTS; i++) mbar_arrive(&s.slot_empty[i]);
+    uint64_t acc[PAIRS][4];  // chain lane j of tokens 2p (low half) and 2p + 1 (high half)
 #pragma unroll
-    for (int t = 0; t < TPW; t++)
+    for (int p = 0; p < PAIRS; p++)
 #pragma unroll
-      for (int j = 0; j < 4; j++) acc[t][j] = 0.0f;
+      for (int j = 0; j < 4; j++) acc[p][j] = 0;
     for (int k = 0; k < kstages; k++) {
-      const int st = k % STAGES;
+      const int st = k % STAGES, slot = k % SLOTS;
       mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 4);
       const int groups = min(4, ng - 4 * k);
-      // the stage's groups' sums of this warp's tokens, then the stage's slot goes back to the MMAs
-      const int slot = k % SLOTS;
+      // the stage's groups' sums of this warp's tokens; magic_bits back in their place for the slot's next MMAs
       mbar_wait(&s.slot_full[slot], (k / SLOTS) & 1, args.error, 5);
       tc_fence_after();
       uint32_t v[4][TPW];
@@ -273,55 +298,81 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < 4; j++)
         if (j < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), v[j]);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        if (j < groups) tmem_st_same<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), magic_bits);
       const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
-      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
       if (4 * k + 4 <= ng4) {
-        // a whole stage below the last four: lane j of the chain takes group 4k + j, no branch in between
+        // a whole stage below the last four: lane j of the chain takes group 4k + j, two tokens at a time
+        const uint32_t wb[4] = {__float_as_uint(w4.x), __float_as_uint(w4.y), __float_as_uint(w4.z),
+                                __float_as_uint(w4.w)};
 #pragma unroll
-        for (int t = 0; t < TPW; t++) {
-          const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
-          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+        for (int j = 0; j < 4; j++) {
+          const uint64_t w2 = pack2(wb[j], wb[j]);
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
-            const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
-            acc[t][j] = __fadd_rn(acc[t][j], __fmul_rn(f, __fmul_rn(wv[j], xv[j])));
+          for (int q = 0; q < TPW / 4; q++) {
+            const uint4 x4 = *reinterpret_cast<const uint4 *>(xrow + j * BN + 4 * q);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              const int p = 2 * q + h;
+              const uint64_t x2 = h ? pack2(x4.z, x4.w) : pack2(x4.x, x4.y);
+              // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
+              const uint64_t f2 = sub2(pack2(v[j][2 * p], v[j][2 * p + 1]), magic2);
+              acc[p][j] = fma2(one2, acc[p][j], mul2(f2, mul2(w2, x2)));
+            }
           }
         }
       } else {
         // the stage with the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int t = 0; t < TPW; t++) {
-          const float4 x4 = *reinterpret_cast<const float4 *>(s.xs[st][sub * TPW + t]);
-          const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-          acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
+        for (int p = 0; p < PAIRS; p++) {
+          float r[2];
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            if (j < groups) {
-              const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
-              acc[t][0] = __fadd_rn(acc[t][0], __fmul_rn(f, __fmul_rn(wv[j], xv[j])));
+          for (int h = 0; h < 2; h++) {
+            const int t = 2 * p + h;
+            float a[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) a[j] = h ? hi(acc[p][j]) : lo(acc[p][j]);
+            float x = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), a[2]), a[3]);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              if (j < groups) {
+                const float f = __fsub_rn(__uint_as_float(v[j][t]), magic);
+                x = __fadd_rn(x, __fmul_rn(f, __fmul_rn(wv[j], xrow[j * BN + t])));
+              }
             }
+            r[h] = x;
           }
+          acc[p][0] = pack2(__float_as_uint(r[0]), __float_as_uint(r[1]));
         }
       }
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.empty[st]);
+      if (lane == 0) {
+        mbar_arrive(&s.slot_empty[slot]);
+        mbar_arrive(&s.empty[st]);
+      }
     }
-    if (ng4 == ng)
+    if (ng4 == ng) {
 #pragma unroll
-      for (int t = 0; t < TPW; t++)
-        acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
+      for (int p = 0; p < PAIRS; p++) {
+        const float r0 = __fadd_rn(__fadd_rn(__fadd_rn(lo(acc[p][0]), lo(acc[p][1])), lo(acc[p][2])), lo(acc[p][3]));
+        const float r1 = __fadd_rn(__fadd_rn(__fadd_rn(hi(acc[p][0]), hi(acc[p][1])), hi(acc[p][2])), hi(acc[p][3]));
+        acc[p][0] = pack2(__float_as_uint(r0), __float_as_uint(r1));
+      }
+    }
     const int r = row0 + rl;
     if (r < args.rows) {
 #pragma unroll
       for (int t = 0; t < TPW; t++) {
         const int tok = tok0 + sub * TPW + t;
         if (tok < args.count) {
+          const float x = (t & 1) ? hi(acc[t >> 1][0]) : lo(acc[t >> 1][0]);
           float *o = args.out + (int64_t)tok * args.out_stride + r;
-          *o = args.accumulate ? __fadd_rn(*o, acc[t][0]) : acc[t][0];
+          *o = args.accumulate ? __fadd_rn(*o, x) : x;
         }
       }
     }
@@ -382,12 +433,19 @@ int make_scale_map(CUtensorMap *map, const float *base, int64_t groups, int64_t 
                   CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+int make_token_scale_map(CUtensorMap *map, const float *base, int64_t tokens, int64_t groups, int64_t row_floats,
+                         int box_tokens) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, tokens, groups, row_floats * 4, box_tokens, 4,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 size_t gemm_smem_bytes() { return sizeof(Smem) + 1024; }
 
 int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &given, int bn, cudaStream_t stream) {
   GemmArgs args = given;
   args.magic_bits = MAGIC_BITS;
   args.magic = MAGIC;
+  args.one = 1.0f;
   if (args.count <= 0 || args.rows <= 0) return 0;
   if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
   if (bn != 16 && bn != 32) return fail(B200FWD_EINVAL, "gemm: BN must be 16 or 32");

@@ -16,9 +16,10 @@ struct GemmArgs {
   int accumulate;    // out += result
   // 0x4B400000 and 12582912.0f, handed over at run time: an int32 S below 2^22 in magnitude is float(S) exactly
   // as (the float with bits S + magic_bits) - magic. (As literals the compiler turns the pair back into a
-  // conversion instruction, a far slower pipe.)
+  // conversion instruction, a far slower pipe.) The tensor cores add S to magic_bits in TMEM.
   uint32_t magic_bits;
   float magic;
+  float one;  // 1.0f, at run time: the chains add as fma(one, acc, product) (gemm_tc.cu, pair helpers)
 };
 
 // the four TMA maps of one matmul
@@ -26,7 +27,7 @@ struct GemmMaps {
   CUtensorMap w;   // int8 weights [rows_total][n]: boxes of 128 bytes x 128 rows (make_i8_map)
   CUtensorMap x;   // int8 activations less the bias [tokens][..]: boxes of 128 bytes x bn tokens
   CUtensorMap ws;  // float32 weight scales [rows_total][stride], stride a multiple of 4: boxes of 4 x 128
-  CUtensorMap xs;  // float32 activation scales [tokens][stride]: boxes of 4 x bn
+  CUtensorMap xs;  // float32 activation scales [groups][stride >= tokens], one row per group: boxes of bn x 4
 };
 
 // int8 rows: cols bytes of rows rows, row_bytes apart; boxes of 128 bytes x box_rows rows, 128-byte swizzle (the
@@ -35,6 +36,10 @@ int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, 
 // float32 scale rows: groups of rows rows, row_floats apart (a multiple of 4); boxes of 4 groups x box_rows
 int make_scale_map(CUtensorMap *map, const float *base, int64_t groups, int64_t rows, int64_t row_floats,
                    int box_rows);
+// float32 activation scales one row per group: tokens of groups rows, row_floats apart (a multiple of 4); boxes of
+// box_tokens tokens x 4 groups
+int make_token_scale_map(CUtensorMap *map, const float *base, int64_t tokens, int64_t groups, int64_t row_floats,
+                         int box_tokens);
 int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream);
 // the kernels' shared-memory opt-in on the current device (before any graph capture)
 int prepare_gemm();

@@ -63,7 +63,7 @@ __device__ __forceinline__ T pick3(int j, T a, T b, T c) { return j == 0 ? a : (
 template <int MT, bool RELAXED>
 __global__ void __launch_bounds__(MV_WARPS * 32)
     matvec_kernel(MatJobs jobs, const int8_t *__restrict__ xq, const float *__restrict__ xs, int64_t q_stride,
-                  int64_t s_stride, int count) {
+                  int64_t s_stride, int64_t g_stride, int count) {
   constexpr int LANES = RELAXED ? 1 : 4;
   __shared__ float buf[MV_WARPS][MT][LANES][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(MV_WARPS * 32)
               const int8_t *xrow = xq + (int64_t)(t0 + t) * q_stride + (int64_t)g * 32;
               const uint4 xa = *reinterpret_cast<const uint4 *>(xrow);
               const uint4 xb = *reinterpret_cast<const uint4 *>(xrow + 16);
-              const float sc = fmul(sw, xs[(int64_t)(t0 + t) * s_stride + g]);
+              const float sc = fmul(sw, xs[(int64_t)(t0 + t) * s_stride + (int64_t)g * g_stride]);
               if (RELAXED) {
                 const int S = dot_group(wa, wb, xa, xb, corr);
                 buf[warp][t][0][lane] = fmul(__int2float_rn(S), sc);
@@ -196,7 +196,7 @@ __device__ __forceinline__ float norm_scale(const float *x, int n, float eps, fl
 }
 
 __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias,
-                                     int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride,
+                                     int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
                                      const int32_t *channels, int nch, float *picked, float *out_f,
                                      int64_t out_stride, int shift) {
   __shared__ float part[5];
@@ -214,7 +214,7 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
         v = 0.0f;
       }
     }
-    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
+    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
   }
 }
 
@@ -237,19 +237,19 @@ __global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh
 }
 
 __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq,
-                                int64_t q_stride, float *xs, int64_t s_stride, int shift) {
+                                int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
   const int lane = threadIdx.x & 31;
   const int ng = n >> 5;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= (int64_t)ng * count) return;
   const int tok = (int)(gw / ng), g = (int)(gw % ng);
   const float v = x[(int64_t)tok * x_stride + g * 32 + lane];
-  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
+  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
 // kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x
 __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int count,
-                                       int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int shift) {
+                                       int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
   const int lane = threadIdx.x & 31;
   const int ng = n >> 5, n4 = n & ~3;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -259,7 +259,7 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
   const float v = h1[(int64_t)tok * stride + j];
   const float e = j < n4 ? vexp(-v) : fexp(-v);
   const float o = fmul(fdiv(v, fadd(1.0f, e)), h3[(int64_t)tok * stride + j]);
-  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + g, shift);
+  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
@@ -391,6 +391,15 @@ __global__ void gather_rows_kernel(float *dst, int64_t dst_stride, const float *
   dst[(int64_t)t * dst_stride + j] = src[(int64_t)idx[t] * src_stride + j];
 }
 
+// scales of count tokens, one row per token (s_stride apart), into one row per group (t_stride apart)
+__global__ void scales_by_group_kernel(float *dst, int64_t t_stride, const float *src, int64_t s_stride, int count,
+                                       int groups) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)count * groups) return;
+  const int g = (int)(i / count), t = (int)(i % count);
+  dst[(int64_t)g * t_stride + t] = src[(int64_t)t * s_stride + g];
+}
+
 __global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                                        const int32_t *channels, int nch) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -454,12 +463,12 @@ inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + thre
 }  // namespace
 
 int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_t q_stride, int64_t s_stride,
-                  int count, bool relaxed, cudaStream_t stream) {
+                  int64_t g_stride, int count, bool relaxed, cudaStream_t stream) {
   if (count <= 0 || jobs.total_rows <= 0) return 0;
   if (jobs.n % 32) return fail(B200FWD_EINVAL, "matvec: n must be whole groups of 32");
   const unsigned grid = std::min<unsigned>(blocks_for(jobs.total_rows, MV_WARPS), 148u * 32u);
   const int mt = count >= 8 ? 8 : count >= 4 ? 4 : count >= 2 ? 2 : 1;
-#define B200_MV(MT, R) matvec_kernel<MT, R><<<grid, MV_WARPS * 32, 0, stream>>>(jobs, xq, xs, q_stride, s_stride, count)
+#define B200_MV(MT, R) matvec_kernel<MT, R><<<grid, MV_WARPS * 32, 0, stream>>>(jobs, xq, xs, q_stride, s_stride, g_stride, count)
   if (relaxed) {
     switch (mt) {
       case 8: B200_MV(8, true); break;
@@ -481,34 +490,35 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
 }
 
 int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
-                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
-                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift) {
+                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, const int32_t *channels,
+                         int nch, float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
-  norm_quantize_kernel<<<count, 256, 0, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, channels,
-                                                  nch, picked, out_f, out_stride, shift);
+  norm_quantize_kernel<<<count, 256, 0, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
+                                                  channels, nch, picked, out_f, out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;
 }
 
 int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
-                    float *xs, int64_t s_stride, cudaStream_t stream, int shift) {
+                    float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "quantize_x: n must be whole groups of 32");
   const int64_t warps = (int64_t)(n / 32) * count;
   quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride,
-                                                            shift);
+                                                            g_stride, shift);
   B200_LAUNCHED("quantize_kernel");
   return 0;
 }
 
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
-                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream, int shift) {
+                           int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream,
+                           int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
   const int64_t warps = (int64_t)(n / 32) * count;
   swiglu_quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq, q_stride, xs,
-                                                                   s_stride, shift);
+                                                                   s_stride, g_stride, shift);
   B200_LAUNCHED("swiglu_quantize_kernel");
   return 0;
 }
@@ -575,6 +585,15 @@ int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t
   gather_rows_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(dst, dst_stride, src, src_stride,
                                                                                 idx, count, dim);
   B200_LAUNCHED("gather_rows_kernel");
+  return 0;
+}
+
+int launch_scales_by_group(float *dst, int64_t t_stride, const float *src, int64_t s_stride, int count, int groups,
+                           cudaStream_t stream) {
+  if (count <= 0 || groups <= 0) return 0;
+  scales_by_group_kernel<<<blocks_for((int64_t)count * groups, 256), 256, 0, stream>>>(dst, t_stride, src, s_stride,
+                                                                                      count, groups);
+  B200_LAUNCHED("scales_by_group_kernel");
   return 0;
 }
 

@@ -29,9 +29,11 @@ struct MatJobs {
   int signed_input;   // the activations are already less the bias (q - 64): a group's integer is dot(w, x)
 };
 
+// Activation scales: token t's group g at xs[t * s_stride + g * g_stride] (one row per token: g_stride 1; the
+// engine's layout, one row per group, which the tensor-core matmul reads: s_stride 1).
 // kernel_relaxed.ts:34-67/164-183 (relaxed) or kernel.ts:231-251 (8-bit): count tokens of activations
 int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_t q_stride, int64_t s_stride,
-                  int count, bool relaxed, cudaStream_t stream);
+                  int64_t g_stride, int count, bool relaxed, cudaStream_t stream);
 
 // The quantizing kernels below store each int8 less `shift` (0: the reference's bytes; 64 with bias 64: q - 64,
 // the signed values whose dot products with the weights are the reference's corrected group integers).
@@ -39,14 +41,16 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
 // device) are taken out of the normalized vector first (forward.js:525-528: picked[c] = value, value = 0).
 // out_f (nullable) also gets the normalized floats.
 int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
-                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, const int32_t *channels, int nch,
-                         float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift = 0);
+                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
+                         const int32_t *channels, int nch, float *picked, float *out_f, int64_t out_stride,
+                         cudaStream_t stream, int shift = 0);
 // kernel.ts:129-156 quantize_x, per token
 int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq, int64_t q_stride,
-                    float *xs, int64_t s_stride, cudaStream_t stream, int shift = 0);
+                    float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream, int shift = 0);
 // kernel.ts:654-667 swiglu then quantize_x of its output, per token
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
-                           int64_t q_stride, float *xs, int64_t s_stride, cudaStream_t stream, int shift = 0);
+                           int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream,
+                           int shift = 0);
 // forward.js:403-414 embed of int8 rows: x[t][i] = w[token*dim+i] * s[token*sstride + i/32]; tokens on the device
 int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim, float *x,
                  int64_t x_stride, cudaStream_t stream);
@@ -73,6 +77,9 @@ int launch_add_columns(float *y, int64_t y_stride, const float *rows, const floa
 // argmax of count rows: mode 0 kernel.ts:695-699 (first index with `>`), mode 1 numpy.argmax (a NaN wins)
 int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count, int mode, cudaStream_t stream);
 // dst[i] = src[idx[i]] (rows of dim floats)
+// activation scales of count tokens from one row per token (s_stride apart) to one row per group (t_stride apart)
+int launch_scales_by_group(float *dst, int64_t t_stride, const float *src, int64_t s_stride, int count, int groups,
+                           cudaStream_t stream);
 int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t src_stride, const int32_t *idx,
                        int count, int dim, cudaStream_t stream);
 // forward.js:799-813 the outlier channels' float32 columns: cols[i][v] = w[v*dim+c_i] * s[v*sstride + c_i/32]

@@ -200,3 +200,23 @@ def test_not_finite_logits_stop_greedy(stories):
         eng.generate_greedy([0], [1], [0], 2)
     assert err.value.code == abi.ENOTFINITE
     eng.forward(1, 0)  # still answers
+
+
+def test_time_matmuls_leaves_the_sequence_alone(stories):
+    """b200fwd_time_matmuls (the bench's roofline leg) writes only scratch: a sequence continued after it gives the
+    logits it gives without it, to the bit; one pass is every layer's four matmuls and the classifier."""
+    data, plan = stories
+    rng = np.random.default_rng(2)
+    prompt = [1] + [int(t) for t in rng.integers(0, 32000, 40)]
+    runs = []
+    for timed in (False, True):
+        eng = Engine(data, plan, slots=2)
+        eng.run([0] * 40 + [1] * 40, prompt[:-1] * 2, list(range(40)) * 2)
+        if timed:
+            ms, nbytes, launches = eng.time_matmuls(32, reps=2)
+            assert ms > 0 and launches == 4 * plan["n_layers"] + 1
+            assert nbytes > plan["vocab_size"] * plan["dim"]
+        last, _ = eng.run([0, 1], [prompt[-1]] * 2, [40, 40], want=[1, 1])
+        runs.append(last)
+        eng.release()
+    assert np.array_equal(bits(runs[0]), bits(runs[1]))

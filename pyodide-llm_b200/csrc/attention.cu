@@ -256,11 +256,157 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
   }
 }
 
+// ---- single query tokens (decode): no tile shares the keys and values, so each thread loads its own straight from
+// the cache (16-byte loads of its position's row for the scores; a pair of values per position for the weighted
+// sum), with no shared-memory staging and no block-wide waits in the loops.
+constexpr int DEC_POS = 128;  // positions of a scores block
+
+template <bool HALF>
+__device__ __forceinline__ void load8(const void *cache, int64_t at, float (&k)[HALF ? 8 : 4]) {
+  if (HALF) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(cache) + at);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      k[2 * i] = half_to_float((uint16_t)(w[i] & 0xffff));
+      k[2 * i + 1] = half_to_float((uint16_t)(w[i] >> 16));
+    }
+  } else {
+    const float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(cache) + at);
+    k[0] = f.x;
+    k[1] = f.y;
+    k[2] = f.z;
+    k[3] = f.w;
+  }
+}
+
+// grid (position blocks of DEC_POS, kv heads, tokens), a thread a position: the same sums as attn_scores_tiled
+// (four lane accumulators over the head's dims, (l0+l2)+(l1+l3), times 1/sqrt(hs)); hs a multiple of the values a
+// 16-byte load holds, so the head has no dims past its fours
+template <bool HALF, int G>
+__global__ void __launch_bounds__(DEC_POS)
+    attn_scores_decode(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
+                       const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
+                       int h1) {
+  extern __shared__ float qs[];  // [G][hs]
+  constexpr int PER = HALF ? 8 : 4;
+  const int kvh = blockIdx.y, tok = blockIdx.z;
+  const int last = pos_of(pos, pos0, tok);
+  const int c0 = blockIdx.x * DEC_POS;
+  if (c0 > last) return;
+  for (int idx = threadIdx.x; idx < G * hs; idx += blockDim.x)
+    qs[idx] = q[(int64_t)tok * q_stride + (int64_t)kvh * G * hs + idx];
+  __syncthreads();
+  const int p = c0 + threadIdx.x;
+  if (p > last) return;
+  const int64_t kvDim = (int64_t)nkv * hs;
+  const int64_t at = (seq ? (int64_t)seq[tok] : 0) * seq_stride + p * kvDim + (int64_t)kvh * hs;
+  float a[G][4];
+#pragma unroll
+  for (int g = 0; g < G; g++) a[g][0] = a[g][1] = a[g][2] = a[g][3] = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < hs; j += PER) {
+    float k[PER];
+    load8<HALF>(kc, at + j, k);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+#pragma unroll
+      for (int u = 0; u < PER; u += 4) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(qs + g * hs + j + u);
+        a[g][0] = fadd(a[g][0], fmul(q4.x, k[u]));
+        a[g][1] = fadd(a[g][1], fmul(q4.y, k[u + 1]));
+        a[g][2] = fadd(a[g][2], fmul(q4.z, k[u + 2]));
+        a[g][3] = fadd(a[g][3], fmul(q4.w, k[u + 3]));
+      }
+    }
+  }
+  const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    const int h = kvh * G + g;
+    if (h < h0 || h >= h1) continue;
+    att[((int64_t)tok * nh + h) * P + p] = fmul(fadd(fadd(a[g][0], a[g][2]), fadd(a[g][1], a[g][3])), isq);
+  }
+}
+
+// grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
+// attn_values_tiled, the positions in fours then one by one; wvec: the weight rows start on 16 bytes
+template <bool HALF, int G>
+__global__ void attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att,
+                                   const int32_t *seq, const int32_t *pos, int pos0, int64_t seq_stride, int P,
+                                   int nh, int nkv, int hs, int h0, int h1, int wvec) {
+  const int kvh = blockIdx.x, tok = blockIdx.y;
+  const int hp = hs / 2, hs4 = hs & ~3;
+  const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
+  const int h = kvh * G + g;
+  if (g >= G || h < h0 || h >= h1) return;
+  const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
+  const int j0 = 2 * jp;
+  const bool four0 = j0 < hs4, four1 = j0 + 1 < hs4;
+  const int64_t kvDim = (int64_t)nkv * hs;
+  const int64_t base = (seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs + j0;
+  const float *w = att + ((int64_t)tok * nh + h) * P;
+  auto pair = [&](int p, float &a, float &b) {
+    const int64_t at = base + p * kvDim;
+    if (HALF) {
+      const uint32_t u = *reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint16_t *>(vc) + at);
+      a = half_to_float((uint16_t)(u & 0xffff));
+      b = half_to_float((uint16_t)(u >> 16));
+    } else {
+      const float2 f = *reinterpret_cast<const float2 *>(reinterpret_cast<const float *>(vc) + at);
+      a = f.x;
+      b = f.y;
+    }
+  };
+  float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll 2
+  for (int p = 0; p < count4; p += 4) {
+    float w0, w1, w2, w3;
+    if (wvec) {
+      const float4 w4 = *reinterpret_cast<const float4 *>(w + p);
+      w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
+    } else {
+      w0 = w[p], w1 = w[p + 1], w2 = w[p + 2], w3 = w[p + 3];
+    }
+    float a[4], b[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) pair(p + u, a[u], b[u]);
+    o0 = four(o0, w0, w1, w2, w3, a[0], a[1], a[2], a[3], four0);
+    o1 = four(o1, w0, w1, w2, w3, b[0], b[1], b[2], b[3], four1);
+  }
+  for (int p = count4; p < count; p++) {
+    float a, b;
+    pair(p, a, b);
+    o0 = fadd(o0, fmul(w[p], a));
+    o1 = fadd(o1, fmul(w[p], b));
+  }
+  float *o = out + (int64_t)tok * out_stride + (int64_t)h * hs + j0;
+  o[0] = o0;
+  o[1] = o1;
+}
+
 template <bool HALF, int G>
 int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                  float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
                  int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int vec,
                  cudaStream_t stream) {
+  const size_t smem_soft = (size_t)max_count * sizeof(float);
+  if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
+  if (!tiles && vec && hs % 2 == 0 && G * (hs / 2) <= 1024) {
+    // one query token a tile: the decode kernels
+    attn_scores_decode<HALF, G><<<dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS,
+                                  (size_t)G * hs * sizeof(float), stream>>>(q, q_stride, kc, att, seq, pos, pos0,
+                                                                            seq_stride, P, nh, nkv, hs, h0, h1);
+    B200_LAUNCHED("attn_scores_decode");
+    attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
+    B200_LAUNCHED("attn_softmax_tiled");
+    const int threads = ((G * (hs / 2) + 31) / 32) * 32;
+    attn_values_decode<HALF, G><<<dim3(nkv, count), threads, 0, stream>>>(
+        out, out_stride, vc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
+        P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0);
+    B200_LAUNCHED("attn_values_decode");
+    return 0;
+  }
   const int chunks = (max_count + ATT_CH - 1) / ATT_CH;
   const int tt = tiles ? ATT_TT : 1;
   const int hsp = (hs + 3) & ~3;
@@ -275,8 +421,6 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
   attn_scores_tiled<HALF, G><<<dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream>>>(
       q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
   B200_LAUNCHED("attn_scores_tiled");
-  const size_t smem_soft = (size_t)max_count * sizeof(float);
-  if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
   attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
   B200_LAUNCHED("attn_softmax_tiled");
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;

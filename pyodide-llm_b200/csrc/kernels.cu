@@ -174,21 +174,35 @@ __device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8
   if (lane == 0) *xs = scale;
 }
 
-// kernel.ts:330-342 rmsnorm's scale: four lane chains over the fours, ((0+1)+2)+3, the rest one by one
-__device__ __forceinline__ float norm_scale(const float *x, int n, float eps, float *part) {
+// kernel.ts:330-342 rmsnorm's scale: four lane chains over the fours, ((0+1)+2)+3, the rest one by one. The whole
+// block squares the vector into shared memory (sq: n floats, each square rounded once as the reference rounds it),
+// then four threads run the lane chains (the chains' adds are the only serial part).
+constexpr int NORM_MAX = 12288;  // the longest vector a block normalizes (its squares fill 48 KB of shared memory)
+__device__ __forceinline__ float norm_scale(const float *x, int n, float eps, float *sq, float *part) {
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float v = x[j];
+    sq[j] = fmul(v, v);
+  }
+  __syncthreads();
   const int n4 = n & ~3;
   if (threadIdx.x < 4) {
+    // sixteen squares read ahead of their adds (the reads do not wait on the chain)
     float acc = 0.0f;
-    for (int j = threadIdx.x; j < n4; j += 4) {
-      const float v = x[j];
-      acc = fadd(acc, fmul(v, v));
+    int j = threadIdx.x;
+    for (; j + 60 < n4; j += 64) {
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) v[u] = sq[j + 4 * u];
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = fadd(acc, v[u]);
     }
+    for (; j < n4; j += 4) acc = fadd(acc, sq[j]);
     part[threadIdx.x] = acc;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     float ss = fadd(fadd(fadd(part[0], part[1]), part[2]), part[3]);
-    for (int j = n4; j < n; j++) ss = fadd(ss, fmul(x[j], x[j]));
+    for (int j = n4; j < n; j++) ss = fadd(ss, sq[j]);
     part[4] = fdiv(1.0f, __fsqrt_rn(fadd(fdiv(ss, (float)n), eps)));
   }
   __syncthreads();
@@ -200,9 +214,10 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
                                      const int32_t *channels, int nch, float *picked, float *out_f,
                                      int64_t out_stride, int shift) {
   __shared__ float part[5];
+  extern __shared__ float sq[];
   const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   const float *xr = x + (int64_t)tok * x_stride;
-  const float s = norm_scale(xr, n, eps, part);
+  const float s = norm_scale(xr, n, eps, sq, part);
   const int ng = n >> 5;
   for (int g = warp; g < ng; g += warps) {
     const int j = g * 32 + lane;
@@ -214,14 +229,16 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
         v = 0.0f;
       }
     }
-    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+    quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
+                   xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
   }
 }
 
 __global__ void rmsnorm_kernel(float *out, const float *x, const float *w, int n, float eps, int64_t stride) {
   __shared__ float part[5];
+  extern __shared__ float sq[];
   const float *xr = x + (int64_t)blockIdx.x * stride;
-  const float s = norm_scale(xr, n, eps, part);
+  const float s = norm_scale(xr, n, eps, sq, part);
   for (int j = threadIdx.x; j < n; j += blockDim.x) out[(int64_t)blockIdx.x * stride + j] = fmul(w[j], fmul(s, xr[j]));
 }
 
@@ -244,7 +261,8 @@ __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bia
   if (gw >= (int64_t)ng * count) return;
   const int tok = (int)(gw / ng), g = (int)(gw % ng);
   const float v = x[(int64_t)tok * x_stride + g * 32 + lane];
-  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+  quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
+                   xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
 // kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x
@@ -259,7 +277,8 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
   const float v = h1[(int64_t)tok * stride + j];
   const float e = j < n4 ? vexp(-v) : fexp(-v);
   const float o = fmul(fdiv(v, fadd(1.0f, e)), h3[(int64_t)tok * stride + j]);
-  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32, xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+  quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
+                   xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
@@ -490,11 +509,13 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
 }
 
 int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias, int count,
-                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, const int32_t *channels,
-                         int nch, float *picked, float *out_f, int64_t out_stride, cudaStream_t stream, int shift) {
+                         int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
+                         const int32_t *channels, int nch, float *picked, float *out_f, int64_t out_stride,
+                         cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
-  norm_quantize_kernel<<<count, 256, 0, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
+  if (n > NORM_MAX) return fail(B200FWD_EUNSUPPORTED, "rmsnorm+quantize: vectors above 12288 values");
+  norm_quantize_kernel<<<count, 256, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
                                                   channels, nch, picked, out_f, out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;
@@ -512,8 +533,8 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
 }
 
 int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int n, int bias, int count, int8_t *xq,
-                           int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream,
-                           int shift) {
+                           int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
+                           cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
   const int64_t warps = (int64_t)(n / 32) * count;
@@ -549,7 +570,8 @@ int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v
 int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps, int count, int64_t stride,
                    cudaStream_t stream) {
   if (count <= 0) return 0;
-  rmsnorm_kernel<<<count, 256, 0, stream>>>(out, x, w, n, eps, stride);
+  if (n > NORM_MAX) return fail(B200FWD_EUNSUPPORTED, "rmsnorm: vectors above 12288 values");
+  rmsnorm_kernel<<<count, 256, (size_t)n * 4, stream>>>(out, x, w, n, eps, stride);
   B200_LAUNCHED("rmsnorm_kernel");
   return 0;
 }

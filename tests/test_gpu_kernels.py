@@ -111,12 +111,12 @@ def test_matmul_q8r_large_random(lib):
                 assert np.array_equal(bits(got[t]), bits(want)), (n, count, t)
 
 
-def matmul_signed(lib, xq7, xs, w, ws, n, count):
+def matmul_signed(lib, xq7, xs, w, ws, n, count, pad=16):
     """b200k_matmul_q8s: activations of quantize_x(bias 64) handed over less the bias; scale rows padded to a
-    multiple of four floats (the tensor cores' TMA rows), as the engine keeps them."""
+    multiple of `pad` floats."""
     rows = w.size // n
     ng = n // 32
-    ngp = (ng + 3) // 4 * 4
+    ngp = (ng + pad - 1) // pad * pad
     qs = ((n + 15) // 16) * 16
     xsg = np.zeros((count, qs), np.int8)
     xsg[:, :n] = (xq7[:count].astype(np.int16) - 64).astype(np.int8)
@@ -131,11 +131,12 @@ def matmul_signed(lib, xq7, xs, w, ws, n, count):
     return host(out)
 
 
-@pytest.mark.parametrize("n,rows", [(4096, 6144), (14336, 300), (288, 768), (160, 200), (4096, 1024), (4096, 64)])
-def test_matmul_tensor_cores(lib, n, rows):
-    """The tensor-core path (count >= 16 tokens) to the bit against the oracle's matmul_q8r, at the 8B and stories
-    shapes and at widths with groups past the fours (288: 9 groups; 160: 5), both token tile widths; 64 rows take
-    the CUDA cores."""
+@pytest.mark.parametrize("n,rows,pad", [(4096, 6144, 4), (14336, 300, 16), (288, 768, 4), (160, 200, 4),
+                                        (4096, 1024, 16), (4096, 64, 4), (608, 384, 4)])
+def test_matmul_tensor_cores(lib, n, rows, pad):
+    """The tile tensor-core kernel (count >= 16 tokens, the natural group order) to the bit against the oracle's
+    matmul_q8r, at the 8B and stories shapes and at widths with groups past the fours (288: 9 groups; 160: 5; 608:
+    19), both token tile widths, scale rows padded to 4 or 16 floats; 64 rows take the CUDA cores."""
     rng = np.random.default_rng(n + rows)
     w = rng.integers(-128, 128, size=rows * n, dtype=np.int8)
     w[:32] = -128
@@ -149,8 +150,8 @@ def test_matmul_tensor_cores(lib, n, rows):
         xq[t], xs[t] = oracle.quantize_x(x[t], 64)
     xq[0, :] = 127
     want = np.stack([oracle.matmul_q8r(xq[t], xs[t], w, ws, wc, n) for t in range(count_max)])
-    for count in (16, 17, 64, 100, 200):
-        got = matmul_signed(lib, xq, xs, w, ws, n, count)
+    for count in (16, 17, 33, 64, 100, 200):
+        got = matmul_signed(lib, xq, xs, w, ws, n, count, pad)
         assert np.array_equal(bits(got), bits(want[:count])), count
 
 

@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--cpu-prompt", type=int, default=16)
     p.add_argument("--cpu-gen", type=int, default=8)
     p.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "stories15m"])
+    p.add_argument("--matmul", default=None, metavar="ROWSxN",
+                   help="time the int8 matmul alone (b200k_matmul_q8s) at ROWSxN with --seqs tokens, one matrix of "
+                        "random weights on the device: the small case the kernel profiles are captured on")
     return p.parse_args()
 
 
@@ -178,6 +181,9 @@ def reference_arm(args):
     return 0
 
 
+TRAFFIC_RATIO = 139.386 / 139.757  # measured DRAM bytes / algorithmic bytes of one decode-shape matmul launch
+
+
 def matmul_roofline(eng, M, peaks, reps=3):
     """The int8 matmul (the dominant kernel) alone, as the engine launches it at the decode step's M tokens: every
     layer's q|k|v, o, w1|w3 and w2, then the classifier (8.9 GB of weights, far beyond L2), back to back on the
@@ -190,7 +196,11 @@ def matmul_roofline(eng, M, peaks, reps=3):
     return {"kernel": "q8_gemm_tc (int8 group-32 matmul, tcgen05, exact order)" if M >= 16 else
             "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": None, "M": M, "per_launch_us": per_launch_s * 1e6, "launches_per_pass": launches,
+            # DRAM bytes per launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one launch of the
+            # 28672 x 4096 matrix at 64 tokens read and wrote 0.997 of its algorithmic bytes (every byte once);
+            # the same ratio over this pass's launches
+            "traffic": TRAFFIC_RATIO * per_launch_bytes, "traffic_source": "ncu, 28672x4096 at 64 tokens, scaled",
+            "M": M, "per_launch_us": per_launch_s * 1e6, "launches_per_pass": launches,
             "algorithmic_bytes_per_launch": per_launch_bytes, "pass_ms": ms}
 
 
@@ -334,10 +344,56 @@ def b200_arm(args):
     return 0
 
 
+def matmul_arm(args):
+    """One matrix (rows x n int8, scales, --seqs tokens of activations) and --warmup + --steps launches of
+    b200k_matmul_q8s on it, timed with CUDA events; prints one line. Holds rows * n * 1.2 bytes on the device."""
+    import ctypes
+
+    import torch
+
+    from b200fwd import abi
+
+    rows, n = (int(v) for v in args.matmul.lower().split("x"))
+    count = args.seqs
+    lib = abi.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ngp = (n // 32 + 3) // 4 * 4
+    w = torch.randint(-127, 128, (rows, n), dtype=torch.int8, device="cuda", generator=g)
+    ws = torch.rand((rows, ngp), device="cuda", generator=g) * 0.019 + 0.001
+    xq = torch.randint(-63, 64, (count, n), dtype=torch.int8, device="cuda", generator=g)
+    xs = torch.rand((count, ngp), device="cuda", generator=g) * 0.1
+    out = torch.empty((count, rows), device="cuda")
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def launch():
+        abi.check(lib.b200k_matmul_q8s(ptr(out), ptr(xq), ptr(xs), ptr(w), ptr(ws), ngp, n, rows, count, rows, n, ngp,
+                                       None), "matmul_q8s")
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    nbytes = rows * n * 9 / 8 + count * n * 9 / 8 + 4 * count * rows
+    ms = float(np.median(times))
+    print(json.dumps({"matmul": f"{rows}x{n}", "tokens": count, "ms_per_call": ms,
+                      "gb_s": nbytes / (ms / 1e3) / 1e9, "note": "per call: the scale copy, the matmul, the "
+                      "error-word read; weights in L2 after the first call (one matrix)"}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.matmul:
+        return matmul_arm(args)
     return b200_arm(args)
 
 

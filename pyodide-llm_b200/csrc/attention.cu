@@ -329,60 +329,147 @@ __global__ void __launch_bounds__(DEC_POS)
   }
 }
 
+// Two float32 lanes at once (PTX .f32x2), each rounded on its own. A paired multiply feeding a paired add can be
+// fused into one fma below PTX; a product that is an operand of fma(one, a, b), `one` = 1.0f handed over at run
+// time, cannot, and one * a + b is a + b rounded once.
+__device__ __forceinline__ uint64_t pk(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int VCH = 64;  // positions of a value chunk
+
 // grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
-// attn_values_tiled, the positions in fours then one by one; wvec: the weight rows start on 16 bytes
+// attn_values_tiled, the positions in fours then one by one. The head's values come in chunks of VCH positions,
+// copied to shared memory asynchronously (cp.async, the next chunk on its way while this one is used), widened to
+// float32 once per block (the reference's half()), then read by the G heads' threads. A four of positions of two
+// neighbouring values is one paired step: ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)), then added to the sum.
+// wvec: the weight rows start on 16 bytes. Shared memory: 8 * VCH * hs bytes.
 template <bool HALF, int G>
-__global__ void attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att,
-                                   const int32_t *seq, const int32_t *pos, int pos0, int64_t seq_stride, int P,
-                                   int nh, int nkv, int hs, int h0, int h1, int wvec) {
+__global__ void __launch_bounds__(1024)
+    attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
+                       const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
+                       int h1, int wvec, float one) {
+  extern __shared__ __align__(16) uint8_t vsm[];
+  constexpr int ES = HALF ? 2 : 4;
   const int kvh = blockIdx.x, tok = blockIdx.y;
   const int hp = hs / 2, hs4 = hs & ~3;
   const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
   const int h = kvh * G + g;
-  if (g >= G || h < h0 || h >= h1) return;
+  const bool active = g < G && h >= h0 && h < h1;
   const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
-  const int j0 = 2 * jp;
-  const bool four0 = j0 < hs4, four1 = j0 + 1 < hs4;
+  const int chunks = (count + VCH - 1) / VCH;
   const int64_t kvDim = (int64_t)nkv * hs;
-  const int64_t base = (seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs + j0;
-  const float *w = att + ((int64_t)tok * nh + h) * P;
-  auto pair = [&](int p, float &a, float &b) {
-    const int64_t at = base + p * kvDim;
-    if (HALF) {
-      const uint32_t u = *reinterpret_cast<const uint32_t *>(reinterpret_cast<const uint16_t *>(vc) + at);
-      a = half_to_float((uint16_t)(u & 0xffff));
-      b = half_to_float((uint16_t)(u >> 16));
-    } else {
-      const float2 f = *reinterpret_cast<const float2 *>(reinterpret_cast<const float *>(vc) + at);
-      a = f.x;
-      b = f.y;
+  const uint8_t *vbase =
+      reinterpret_cast<const uint8_t *>(vc) + ((seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs) * ES;
+  const int row_bytes = hs * ES, pieces = row_bytes / 16;
+  uint8_t *raw0 = vsm, *raw1 = vsm + VCH * row_bytes;
+  float *wide = reinterpret_cast<float *>(vsm + 2 * VCH * row_bytes);  // the chunk in float32 (HALF)
+  auto issue = [&](int c) {
+    const int r0 = c * VCH, rows = min(VCH, count - r0);
+    uint8_t *dst = (c & 1) ? raw1 : raw0;
+    for (int i = threadIdx.x; i < rows * pieces; i += blockDim.x) {
+      const int r = i / pieces, q = i % pieces;
+      cp_async16(dst + r * row_bytes + q * 16, vbase + (int64_t)(r0 + r) * kvDim * ES + q * 16);
     }
+    cp_async_commit();
   };
-  float o0 = 0.0f, o1 = 0.0f;
-#pragma unroll 2
-  for (int p = 0; p < count4; p += 4) {
-    float w0, w1, w2, w3;
-    if (wvec) {
-      const float4 w4 = *reinterpret_cast<const float4 *>(w + p);
-      w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
+  const int j0 = 2 * jp;
+  const bool fours = j0 < hs4;  // both of the thread's values lie in the head's fours (hs4 and j0 even)
+  const float *w = att + ((int64_t)tok * nh + h) * P;
+  const uint64_t one2 = pk(one, one);
+  uint64_t o = 0;  // the two values' sums
+  issue(0);
+  for (int c = 0; c < chunks; c++) {
+    if (c + 1 < chunks) {
+      issue(c + 1);
+      cp_async_wait<1>();
     } else {
-      w0 = w[p], w1 = w[p + 1], w2 = w[p + 2], w3 = w[p + 3];
+      cp_async_wait<0>();
     }
-    float a[4], b[4];
-#pragma unroll
-    for (int u = 0; u < 4; u++) pair(p + u, a[u], b[u]);
-    o0 = four(o0, w0, w1, w2, w3, a[0], a[1], a[2], a[3], four0);
-    o1 = four(o1, w0, w1, w2, w3, b[0], b[1], b[2], b[3], four1);
+    __syncthreads();  // chunk c is in shared memory, every thread's copies of it
+    const int r0 = c * VCH, rows = min(VCH, count - r0);
+    const float *vf;
+    if (HALF) {
+      const uint32_t *src = reinterpret_cast<const uint32_t *>((c & 1) ? raw1 : raw0);
+      const uint64_t big = pk(5.192296858534828e33f, 5.192296858534828e33f);  // 2^112
+      for (int i = threadIdx.x; i < rows * hp; i += blockDim.x) {
+        const uint32_t u = src[i];
+        const int32_t a = (((int32_t)(int16_t)(u & 0xffff)) << 13) & (int32_t)0x8fffffff;
+        const int32_t b = (((int32_t)(int16_t)(u >> 16)) << 13) & (int32_t)0x8fffffff;
+        reinterpret_cast<uint64_t *>(wide)[i] = mul2(pk(__int_as_float(a), __int_as_float(b)), big);
+      }
+      __syncthreads();
+      vf = wide;
+    } else {
+      vf = reinterpret_cast<const float *>((c & 1) ? raw1 : raw0);
+    }
+    if (active) {
+      for (int i = 0; i < rows; i += 4) {
+        const int p = r0 + i;
+        if (p + 4 <= count4) {
+          float w0, w1, w2, w3;
+          if (wvec) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(w + p);
+            w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
+          } else {
+            w0 = w[p], w1 = w[p + 1], w2 = w[p + 2], w3 = w[p + 3];
+          }
+          const uint64_t v0 = *reinterpret_cast<const uint64_t *>(vf + (i + 0) * hs + j0);
+          const uint64_t v1 = *reinterpret_cast<const uint64_t *>(vf + (i + 1) * hs + j0);
+          const uint64_t v2 = *reinterpret_cast<const uint64_t *>(vf + (i + 2) * hs + j0);
+          const uint64_t v3 = *reinterpret_cast<const uint64_t *>(vf + (i + 3) * hs + j0);
+          if (fours) {
+            const uint64_t s01 = fma2(one2, mul2(pk(w0, w0), v0), mul2(pk(w1, w1), v1));
+            const uint64_t s23 = fma2(one2, mul2(pk(w2, w2), v2), mul2(pk(w3, w3), v3));
+            o = fma2(one2, o, fma2(one2, s01, s23));
+          } else {
+            const float a0 = four(lo(o), w0, w1, w2, w3, lo(v0), lo(v1), lo(v2), lo(v3), false);
+            const float a1 = four(hi(o), w0, w1, w2, w3, hi(v0), hi(v1), hi(v2), hi(v3), false);
+            o = pk(a0, a1);
+          }
+        } else {
+          // the positions past the fours, one at a time (kernel.ts:548-564)
+          float a0 = lo(o), a1 = hi(o);
+          for (int u = 0; u < 4 && p + u < count; u++) {
+            const float2 v = *reinterpret_cast<const float2 *>(vf + (i + u) * hs + j0);
+            a0 = fadd(a0, fmul(w[p + u], v.x));
+            a1 = fadd(a1, fmul(w[p + u], v.y));
+          }
+          o = pk(a0, a1);
+        }
+      }
+    }
+    __syncthreads();  // chunk c's buffers are free for chunk c + 2
   }
-  for (int p = count4; p < count; p++) {
-    float a, b;
-    pair(p, a, b);
-    o0 = fadd(o0, fmul(w[p], a));
-    o1 = fadd(o1, fmul(w[p], b));
+  if (active) {
+    float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + j0;
+    dst[0] = lo(o);
+    dst[1] = hi(o);
   }
-  float *o = out + (int64_t)tok * out_stride + (int64_t)h * hs + j0;
-  o[0] = o0;
-  o[1] = o1;
 }
 
 template <bool HALF, int G>
@@ -401,9 +488,13 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");
     const int threads = ((G * (hs / 2) + 31) / 32) * 32;
-    attn_values_decode<HALF, G><<<dim3(nkv, count), threads, 0, stream>>>(
+    const size_t smem_values = (size_t)8 * VCH * hs;
+    if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
+    B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)MAX_TILE_SMEM));
+    attn_values_decode<HALF, G><<<dim3(nkv, count), threads, smem_values, stream>>>(
         out, out_stride, vc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
-        P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0);
+        P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0, 1.0f);
     B200_LAUNCHED("attn_values_decode");
     return 0;
   }

@@ -101,11 +101,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(int bn) {
          | ((uint32_t)(BM >> 4) << 24);    // M >> 4
 }
 
-// D += A x B: TMEM holds magic_bits before a group's first and only MMA, so D = magic_bits + the group's sum
+// D = A x B (each group's MMA writes its own column block)
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.eq.b32 p, 0, 0;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc)
       : "memory");
@@ -118,7 +118,6 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Two float32 lanes at once (PTX .f32x2), each lane rounded on its own. A paired multiply whose product feeds a
 // paired add is fused into one fma below PTX (one rounding: not the reference's number); a product that is the addend
@@ -177,24 +176,10 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
-// the same word into TPW consecutive TMEM columns of this warp's 32 lanes
-template <int TPW>
-__device__ __forceinline__ void tmem_st_same(uint32_t taddr, uint32_t v);
-template <>
-__device__ __forceinline__ void tmem_st_same<8>(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(v)
-               : "memory");
-}
-template <>
-__device__ __forceinline__ void tmem_st_same<4>(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(v) : "memory");
-}
-
 // Warp roles: 0 TMA producer, 1 MMA issue, 2..17 epilogue. Epilogue warp w reads TMEM lane quarter w % 4 (its 32
 // rows) and token columns (w - 2) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
 // its (row, token) in registers, two tokens to a 64-bit pair: the chains, their sum and the groups past the fours
-// all happen in one thread. It also puts magic_bits back into the TMEM columns it has read, for the MMAs that reuse
-// them (D = magic_bits + the group's sum: its float is then one paired subtraction).
+// all happen in one thread. A group's sum S becomes float(S) as (the float with bits S + magic_bits) - magic.
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
@@ -247,13 +232,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---- MMA issue: a stage's four groups, one MMA each (K = 32, one group) into four TMEM column blocks of the
-    // stage's slot, one commit per stage. A slot is free once every epilogue warp has read it and put magic_bits
-    // back (the first time: the epilogue's initial fill).
+    // stage's slot, one commit per stage. A slot is free once every epilogue warp has read it.
     const uint32_t idesc = idesc_i8(BN);
     for (int k = 0; k < kstages; k++) {
       const int st = k % STAGES, slot = k % SLOTS;
       if (!mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 2)) break;
-      if (!mbar_wait(&s.slot_empty[slot], (k / SLOTS) & 1, args.error, 3)) break;
+      if (!mbar_wait(&s.slot_empty[slot], ((k / SLOTS) & 1) ^ 1, args.error, 3)) break;
       tc_fence_after();
       if (lane == 0) {
         const int groups = min(4, ng - 4 * k);
@@ -273,14 +257,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint64_t one2 = pack2(__float_as_uint(args.one), __float_as_uint(args.one));
     const int rl = quarter * 32 + lane;  // the row within the tile
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
-    // every slot's columns of this warp start as magic_bits
-#pragma unroll 1
-    for (int c = 0; c < 4 * SLOTS; c++) tmem_st_same<TPW>(taddr + (uint32_t)(c * BN), magic_bits);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0)
-      for (int i = 0; i < SLOTS; i++) mbar_arrive(&s.slot_empty[i]);
     uint64_t acc[PAIRS][4];  // chain lane j of tokens 2p (low half) and 2p + 1 (high half)
 #pragma unroll
     for (int p = 0; p < PAIRS; p++)
@@ -290,7 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int st = k % STAGES, slot = k % SLOTS;
       mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 4);
       const int groups = min(4, ng - 4 * k);
-      // the stage's groups' sums of this warp's tokens; magic_bits back in their place for the slot's next MMAs
+      // the stage's groups' sums of this warp's tokens, then the slot goes back to the MMAs
       mbar_wait(&s.slot_full[slot], (k / SLOTS) & 1, args.error, 5);
       tc_fence_after();
       uint32_t v[4][TPW];
@@ -298,9 +274,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < 4; j++)
         if (j < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), v[j]);
       tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-        if (j < groups) tmem_st_same<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), magic_bits);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
       const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
       const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
       if (4 * k + 4 <= ng4) {
@@ -318,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int p = 2 * q + h;
               const uint64_t x2 = h ? pack2(x4.z, x4.w) : pack2(x4.x, x4.y);
               // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
-              const uint64_t f2 = sub2(pack2(v[j][2 * p], v[j][2 * p + 1]), magic2);
+              const uint64_t f2 = sub2(pack2(v[j][2 * p] + magic_bits, v[j][2 * p + 1] + magic_bits), magic2);
               acc[p][j] = fma2(one2, acc[p][j], mul2(f2, mul2(w2, x2)));
             }
           }
@@ -339,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 4; j++) {
               if (j < groups) {
-                const float f = __fsub_rn(__uint_as_float(v[j][t]), magic);
+                const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
                 x = __fadd_rn(x, __fmul_rn(f, __fmul_rn(wv[j], xrow[j * BN + t])));
               }
             }
@@ -348,13 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           acc[p][0] = pack2(__float_as_uint(r[0]), __float_as_uint(r[1]));
         }
       }
-      tmem_wait_st();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s.slot_empty[slot]);
-        mbar_arrive(&s.empty[st]);
-      }
+      if (lane == 0) mbar_arrive(&s.empty[st]);
     }
     if (ng4 == ng) {
 #pragma unroll

@@ -16,7 +16,7 @@ struct GemmArgs {
   int accumulate;    // out += result
   // 0x4B400000 and 12582912.0f, handed over at run time: an int32 S below 2^22 in magnitude is float(S) exactly
   // as (the float with bits S + magic_bits) - magic. (As literals the compiler turns the pair back into a
-  // conversion instruction, a far slower pipe.) The tensor cores add S to magic_bits in TMEM.
+  // conversion instruction, a far slower pipe.)
   uint32_t magic_bits;
   float magic;
   float one;  // 1.0f, at run time: the chains add as fma(one, acc, product) (gemm_tc.cu, pair helpers)

@@ -365,9 +365,10 @@ constexpr int VCH = 64;  // positions of a value chunk
 // grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
 // attn_values_tiled, the positions in fours then one by one. The head's values come in chunks of VCH positions,
 // copied to shared memory asynchronously (cp.async, the next chunk on its way while this one is used), widened to
-// float32 once per block (the reference's half()), then read by the G heads' threads. A four of positions of two
-// neighbouring values is one paired step: ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)), then added to the sum.
-// wvec: the weight rows start on 16 bytes. Shared memory: 8 * VCH * hs bytes.
+// float32 once per block (the reference's half()), then read by the G heads' threads; the chunk's softmax weights
+// of the G heads come along the same way. A four of positions of two neighbouring values is one paired step:
+// ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)), then added to the sum. wvec: the weight rows start on 16 bytes.
+// Shared memory: 8 * VCH * hs + 8 * G * VCH bytes.
 template <bool HALF, int G>
 __global__ void __launch_bounds__(1024)
     attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
@@ -388,6 +389,8 @@ __global__ void __launch_bounds__(1024)
   const int row_bytes = hs * ES, pieces = row_bytes / 16;
   uint8_t *raw0 = vsm, *raw1 = vsm + VCH * row_bytes;
   float *wide = reinterpret_cast<float *>(vsm + 2 * VCH * row_bytes);  // the chunk in float32 (HALF)
+  float *wts = reinterpret_cast<float *>(vsm + 8 * VCH * hs);            // [2][G][VCH]: the chunks' weights
+  const float *watt = att + ((int64_t)tok * nh + (int64_t)kvh * G) * P;  // head kvh * G + gg's row at gg * P
   auto issue = [&](int c) {
     const int r0 = c * VCH, rows = min(VCH, count - r0);
     uint8_t *dst = (c & 1) ? raw1 : raw0;
@@ -395,11 +398,22 @@ __global__ void __launch_bounds__(1024)
       const int r = i / pieces, q = i % pieces;
       cp_async16(dst + r * row_bytes + q * 16, vbase + (int64_t)(r0 + r) * kvDim * ES + q * 16);
     }
+    float *wd = wts + (c & 1) * G * VCH;
+    if (wvec && rows % 4 == 0) {
+      for (int i = threadIdx.x; i < G * rows / 4; i += blockDim.x) {
+        const int gg = i / (rows / 4), r = 4 * (i % (rows / 4));
+        cp_async16(wd + gg * VCH + r, watt + (int64_t)gg * P + r0 + r);
+      }
+    } else {
+      for (int i = threadIdx.x; i < G * rows; i += blockDim.x) {
+        const int gg = i / rows, r = i % rows;
+        wd[gg * VCH + r] = watt[(int64_t)gg * P + r0 + r];
+      }
+    }
     cp_async_commit();
   };
   const int j0 = 2 * jp;
   const bool fours = j0 < hs4;  // both of the thread's values lie in the head's fours (hs4 and j0 even)
-  const float *w = att + ((int64_t)tok * nh + h) * P;
   const uint64_t one2 = pk(one, one);
   uint64_t o = 0;  // the two values' sums
   issue(0);
@@ -428,16 +442,12 @@ __global__ void __launch_bounds__(1024)
       vf = reinterpret_cast<const float *>((c & 1) ? raw1 : raw0);
     }
     if (active) {
+      const float *w = wts + (c & 1) * G * VCH + g * VCH;  // this head's weights of the chunk
       for (int i = 0; i < rows; i += 4) {
         const int p = r0 + i;
         if (p + 4 <= count4) {
-          float w0, w1, w2, w3;
-          if (wvec) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(w + p);
-            w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
-          } else {
-            w0 = w[p], w1 = w[p + 1], w2 = w[p + 2], w3 = w[p + 3];
-          }
+          const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
+          const float w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
           const uint64_t v0 = *reinterpret_cast<const uint64_t *>(vf + (i + 0) * hs + j0);
           const uint64_t v1 = *reinterpret_cast<const uint64_t *>(vf + (i + 1) * hs + j0);
           const uint64_t v2 = *reinterpret_cast<const uint64_t *>(vf + (i + 2) * hs + j0);
@@ -456,8 +466,8 @@ __global__ void __launch_bounds__(1024)
           float a0 = lo(o), a1 = hi(o);
           for (int u = 0; u < 4 && p + u < count; u++) {
             const float2 v = *reinterpret_cast<const float2 *>(vf + (i + u) * hs + j0);
-            a0 = fadd(a0, fmul(w[p + u], v.x));
-            a1 = fadd(a1, fmul(w[p + u], v.y));
+            a0 = fadd(a0, fmul(w[i + u], v.x));
+            a1 = fadd(a1, fmul(w[i + u], v.y));
           }
           o = pk(a0, a1);
         }
@@ -488,7 +498,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");
     const int threads = ((G * (hs / 2) + 31) / 32) * 32;
-    const size_t smem_values = (size_t)8 * VCH * hs;
+    const size_t smem_values = (size_t)8 * VCH * hs + (size_t)8 * G * VCH;
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));

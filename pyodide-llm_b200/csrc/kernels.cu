@@ -515,7 +515,9 @@ int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
   if (n > NORM_MAX) return fail(B200FWD_EUNSUPPORTED, "rmsnorm+quantize: vectors above 12288 values");
-  norm_quantize_kernel<<<count, 256, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
+  // a block per token, 32 warps: the squares and the groups' quantization spread over the whole block (only the four
+  // lane chains of the norm are serial)
+  norm_quantize_kernel<<<count, 1024, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
                                                   channels, nch, picked, out_f, out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;

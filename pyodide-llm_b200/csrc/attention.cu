@@ -47,6 +47,37 @@ __device__ __forceinline__ Tile tile_of(const int32_t *tiles, int i) {
 }
 __device__ __forceinline__ int pos_of(const int32_t *pos, int pos0, int tok) { return pos ? pos[tok] : pos0; }
 
+// Two float32 lanes at once (PTX .f32x2), each rounded on its own. A paired multiply feeding a paired add can be
+// fused into one fma below PTX; a product that is an operand of fma(one, a, b), `one` = 1.0f handed over at run
+// time, cannot, and one * a + b is a + b rounded once.
+__device__ __forceinline__ uint64_t pk(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // positions c0..c0+rows-1 of one kv head of one sequence's cache, as float32, into dst rows `pitch` floats apart
 template <bool HALF>
 __device__ __forceinline__ void stage_rows(float *dst, int pitch, const void *cache, int64_t row0, int64_t kvDim,
@@ -261,25 +292,6 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
 // sum), with no shared-memory staging and no block-wide waits in the loops.
 constexpr int DEC_POS = 128;  // positions of a scores block
 
-template <bool HALF>
-__device__ __forceinline__ void load8(const void *cache, int64_t at, float (&k)[HALF ? 8 : 4]) {
-  if (HALF) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(cache) + at);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      k[2 * i] = half_to_float((uint16_t)(w[i] & 0xffff));
-      k[2 * i + 1] = half_to_float((uint16_t)(w[i] >> 16));
-    }
-  } else {
-    const float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(cache) + at);
-    k[0] = f.x;
-    k[1] = f.y;
-    k[2] = f.z;
-    k[3] = f.w;
-  }
-}
-
 // grid (position blocks of DEC_POS, kv heads, tokens), a thread a position: the same sums as attn_scores_tiled
 // (four lane accumulators over the head's dims, (l0+l2)+(l1+l3), times 1/sqrt(hs)); hs a multiple of the values a
 // 16-byte load holds, so the head has no dims past its fours
@@ -287,7 +299,7 @@ template <bool HALF, int G>
 __global__ void __launch_bounds__(DEC_POS)
     attn_scores_decode(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
                        const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
-                       int h1) {
+                       int h1, float one) {
   extern __shared__ float qs[];  // [G][hs]
   constexpr int PER = HALF ? 8 : 4;
   const int kvh = blockIdx.y, tok = blockIdx.z;
@@ -301,22 +313,36 @@ __global__ void __launch_bounds__(DEC_POS)
   if (p > last) return;
   const int64_t kvDim = (int64_t)nkv * hs;
   const int64_t at = (seq ? (int64_t)seq[tok] : 0) * seq_stride + p * kvDim + (int64_t)kvh * hs;
-  float a[G][4];
+  const uint64_t one2 = pk(one, one);
+  // lane accumulators (0, 1) and (2, 3) of each head, paired: lane k takes the dims 4i + k
+  uint64_t a01[G], a23[G];
 #pragma unroll
-  for (int g = 0; g < G; g++) a[g][0] = a[g][1] = a[g][2] = a[g][3] = 0.0f;
+  for (int g = 0; g < G; g++) a01[g] = a23[g] = 0;
 #pragma unroll 4
   for (int j = 0; j < hs; j += PER) {
-    float k[PER];
-    load8<HALF>(kc, at + j, k);
+    uint64_t k2[PER / 2];  // this position's keys j .. j + PER - 1 in pairs
+    if (HALF) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(kc) + at + j);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      const uint64_t big = pk(5.192296858534828e33f, 5.192296858534828e33f);  // 2^112: the reference's half()
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int32_t lo16 = (((int32_t)(int16_t)(w[i] & 0xffff)) << 13) & (int32_t)0x8fffffff;
+        const int32_t hi16 = (((int32_t)(int16_t)(w[i] >> 16)) << 13) & (int32_t)0x8fffffff;
+        k2[i] = mul2(pk(__int_as_float(lo16), __int_as_float(hi16)), big);
+      }
+    } else {
+      const ulonglong2 f = *reinterpret_cast<const ulonglong2 *>(reinterpret_cast<const float *>(kc) + at + j);
+      k2[0] = f.x;
+      k2[1] = f.y;
+    }
 #pragma unroll
     for (int g = 0; g < G; g++) {
 #pragma unroll
       for (int u = 0; u < PER; u += 4) {
-        const float4 q4 = *reinterpret_cast<const float4 *>(qs + g * hs + j + u);
-        a[g][0] = fadd(a[g][0], fmul(q4.x, k[u]));
-        a[g][1] = fadd(a[g][1], fmul(q4.y, k[u + 1]));
-        a[g][2] = fadd(a[g][2], fmul(q4.z, k[u + 2]));
-        a[g][3] = fadd(a[g][3], fmul(q4.w, k[u + 3]));
+        const ulonglong2 q4 = *reinterpret_cast<const ulonglong2 *>(qs + g * hs + j + u);
+        a01[g] = fma2(one2, a01[g], mul2(q4.x, k2[u / 2]));
+        a23[g] = fma2(one2, a23[g], mul2(q4.y, k2[u / 2 + 1]));
       }
     }
   }
@@ -325,42 +351,12 @@ __global__ void __launch_bounds__(DEC_POS)
   for (int g = 0; g < G; g++) {
     const int h = kvh * G + g;
     if (h < h0 || h >= h1) continue;
-    att[((int64_t)tok * nh + h) * P + p] = fmul(fadd(fadd(a[g][0], a[g][2]), fadd(a[g][1], a[g][3])), isq);
+    const float s4 = fadd(fadd(lo(a01[g]), lo(a23[g])), fadd(hi(a01[g]), hi(a23[g])));  // (l0+l2)+(l1+l3)
+    att[((int64_t)tok * nh + h) * P + p] = fmul(s4, isq);
   }
 }
 
-// Two float32 lanes at once (PTX .f32x2), each rounded on its own. A paired multiply feeding a paired add can be
-// fused into one fma below PTX; a product that is an operand of fma(one, a, b), `one` = 1.0f handed over at run
-// time, cannot, and one * a + b is a + b rounded once.
-__device__ __forceinline__ uint64_t pk(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
-
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-constexpr int VCH = 64;  // positions of a value chunk
+constexpr int VCH = 32;  // positions of a value chunk
 
 // grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
 // attn_values_tiled, the positions in fours then one by one. The head's values come in chunks of VCH positions,
@@ -493,7 +489,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     // one query token a tile: the decode kernels
     attn_scores_decode<HALF, G><<<dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS,
                                   (size_t)G * hs * sizeof(float), stream>>>(q, q_stride, kc, att, seq, pos, pos0,
-                                                                            seq_stride, P, nh, nkv, hs, h0, h1);
+                                                                            seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
     B200_LAUNCHED("attn_scores_decode");
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");

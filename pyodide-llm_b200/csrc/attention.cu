@@ -300,19 +300,30 @@ __global__ void __launch_bounds__(DEC_POS)
     attn_scores_decode(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
                        const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
                        int h1, float one) {
-  extern __shared__ float qs[];  // [G][hs]
-  constexpr int PER = HALF ? 8 : 4;
+  extern __shared__ __align__(16) float qs[];  // [G][hs], then the chunk's keys: DEC_POS rows of hs * ES + 16 bytes
+  constexpr int PER = HALF ? 8 : 4, ES = HALF ? 2 : 4;
   const int kvh = blockIdx.y, tok = blockIdx.z;
   const int last = pos_of(pos, pos0, tok);
   const int c0 = blockIdx.x * DEC_POS;
   if (c0 > last) return;
+  const int rows = min(DEC_POS, last + 1 - c0);
+  const int64_t kvDim = (int64_t)nkv * hs;
+  const int row_bytes = hs * ES, pitch = row_bytes + 16, pieces = row_bytes / 16;  // pitch: rows 4 banks apart
+  uint8_t *ks = reinterpret_cast<uint8_t *>(qs + G * hs);
+  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(kc) +
+                         ((seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs) * ES;
+  for (int i = threadIdx.x; i < rows * pieces; i += blockDim.x) {
+    const int r = i / pieces, c = i % pieces;
+    cp_async16(ks + r * pitch + c * 16, kbase + (int64_t)r * kvDim * ES + c * 16);
+  }
+  cp_async_commit();
   for (int idx = threadIdx.x; idx < G * hs; idx += blockDim.x)
     qs[idx] = q[(int64_t)tok * q_stride + (int64_t)kvh * G * hs + idx];
+  cp_async_wait<0>();
   __syncthreads();
   const int p = c0 + threadIdx.x;
   if (p > last) return;
-  const int64_t kvDim = (int64_t)nkv * hs;
-  const int64_t at = (seq ? (int64_t)seq[tok] : 0) * seq_stride + p * kvDim + (int64_t)kvh * hs;
+  const uint8_t *krow = ks + threadIdx.x * pitch;
   const uint64_t one2 = pk(one, one);
   // lane accumulators (0, 1) and (2, 3) of each head, paired: lane k takes the dims 4i + k
   uint64_t a01[G], a23[G];
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(DEC_POS)
   for (int j = 0; j < hs; j += PER) {
     uint64_t k2[PER / 2];  // this position's keys j .. j + PER - 1 in pairs
     if (HALF) {
-      const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(kc) + at + j);
+      const uint4 u = *reinterpret_cast<const uint4 *>(krow + j * 2);
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
       const uint64_t big = pk(5.192296858534828e33f, 5.192296858534828e33f);  // 2^112: the reference's half()
 #pragma unroll
@@ -332,7 +343,7 @@ __global__ void __launch_bounds__(DEC_POS)
         k2[i] = mul2(pk(__int_as_float(lo16), __int_as_float(hi16)), big);
       }
     } else {
-      const ulonglong2 f = *reinterpret_cast<const ulonglong2 *>(reinterpret_cast<const float *>(kc) + at + j);
+      const ulonglong2 f = *reinterpret_cast<const ulonglong2 *>(krow + j * 4);
       k2[0] = f.x;
       k2[1] = f.y;
     }
@@ -357,14 +368,20 @@ __global__ void __launch_bounds__(DEC_POS)
 }
 
 constexpr int VCH = 32;  // positions of a value chunk
+constexpr int VNB = 4;   // value chunks in flight (shared-memory buffers)
+
+// shared memory of attn_values_decode: VNB raw chunks, the widened chunk (float16 caches), VNB chunks of weights
+inline size_t values_smem(int hs, int G, bool half) {
+  return (size_t)VNB * VCH * hs * (half ? 2 : 4) + (half ? (size_t)VCH * hs * 4 : 0) + (size_t)VNB * G * VCH * 4;
+}
 
 // grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
 // attn_values_tiled, the positions in fours then one by one. The head's values come in chunks of VCH positions,
 // copied to shared memory asynchronously (cp.async, the next chunk on its way while this one is used), widened to
 // float32 once per block (the reference's half()), then read by the G heads' threads; the chunk's softmax weights
-// of the G heads come along the same way. A four of positions of two neighbouring values is one paired step:
-// ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)), then added to the sum. wvec: the weight rows start on 16 bytes.
-// Shared memory: 8 * VCH * hs + 8 * G * VCH bytes.
+// of the G heads come along the same way, VNB - 1 chunks ahead. A four of positions of two neighbouring values is
+// one paired step: ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)), then added to the sum. wvec: the weight rows start on 16
+// bytes. Shared memory: values_smem(hs, G, HALF).
 template <bool HALF, int G>
 __global__ void __launch_bounds__(1024)
     attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
@@ -383,18 +400,18 @@ __global__ void __launch_bounds__(1024)
   const uint8_t *vbase =
       reinterpret_cast<const uint8_t *>(vc) + ((seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs) * ES;
   const int row_bytes = hs * ES, pieces = row_bytes / 16;
-  uint8_t *raw0 = vsm, *raw1 = vsm + VCH * row_bytes;
-  float *wide = reinterpret_cast<float *>(vsm + 2 * VCH * row_bytes);  // the chunk in float32 (HALF)
-  float *wts = reinterpret_cast<float *>(vsm + 8 * VCH * hs);            // [2][G][VCH]: the chunks' weights
+  float *wide = reinterpret_cast<float *>(vsm + VNB * VCH * row_bytes);  // the chunk in float32 (HALF)
+  float *wts = reinterpret_cast<float *>(vsm + VNB * VCH * row_bytes + (HALF ? VCH * hs * 4 : 0));  // [VNB][G][VCH]
   const float *watt = att + ((int64_t)tok * nh + (int64_t)kvh * G) * P;  // head kvh * G + gg's row at gg * P
+  // chunk c's values and weights into buffer c % VNB, one commit group per call (empty past the last chunk)
   auto issue = [&](int c) {
-    const int r0 = c * VCH, rows = min(VCH, count - r0);
-    uint8_t *dst = (c & 1) ? raw1 : raw0;
+    const int r0 = c * VCH, rows = max(0, min(VCH, count - r0));
+    uint8_t *dst = vsm + (c % VNB) * VCH * row_bytes;
     for (int i = threadIdx.x; i < rows * pieces; i += blockDim.x) {
       const int r = i / pieces, q = i % pieces;
       cp_async16(dst + r * row_bytes + q * 16, vbase + (int64_t)(r0 + r) * kvDim * ES + q * 16);
     }
-    float *wd = wts + (c & 1) * G * VCH;
+    float *wd = wts + (c % VNB) * G * VCH;
     if (wvec && rows % 4 == 0) {
       for (int i = threadIdx.x; i < G * rows / 4; i += blockDim.x) {
         const int gg = i / (rows / 4), r = 4 * (i % (rows / 4));
@@ -412,19 +429,15 @@ __global__ void __launch_bounds__(1024)
   const bool fours = j0 < hs4;  // both of the thread's values lie in the head's fours (hs4 and j0 even)
   const uint64_t one2 = pk(one, one);
   uint64_t o = 0;  // the two values' sums
-  issue(0);
+  for (int c = 0; c + 1 < VNB; c++) issue(c);
   for (int c = 0; c < chunks; c++) {
-    if (c + 1 < chunks) {
-      issue(c + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    issue(c + VNB - 1);
+    cp_async_wait<VNB - 1>();
     __syncthreads();  // chunk c is in shared memory, every thread's copies of it
     const int r0 = c * VCH, rows = min(VCH, count - r0);
     const float *vf;
     if (HALF) {
-      const uint32_t *src = reinterpret_cast<const uint32_t *>((c & 1) ? raw1 : raw0);
+      const uint32_t *src = reinterpret_cast<const uint32_t *>(vsm + (c % VNB) * VCH * row_bytes);
       const uint64_t big = pk(5.192296858534828e33f, 5.192296858534828e33f);  // 2^112
       for (int i = threadIdx.x; i < rows * hp; i += blockDim.x) {
         const uint32_t u = src[i];
@@ -435,10 +448,10 @@ __global__ void __launch_bounds__(1024)
       __syncthreads();
       vf = wide;
     } else {
-      vf = reinterpret_cast<const float *>((c & 1) ? raw1 : raw0);
+      vf = reinterpret_cast<const float *>(vsm + (c % VNB) * VCH * row_bytes);
     }
     if (active) {
-      const float *w = wts + (c & 1) * G * VCH + g * VCH;  // this head's weights of the chunk
+      const float *w = wts + (c % VNB) * G * VCH + g * VCH;  // this head's weights of the chunk
       for (int i = 0; i < rows; i += 4) {
         const int p = r0 + i;
         if (p + 4 <= count4) {
@@ -469,7 +482,7 @@ __global__ void __launch_bounds__(1024)
         }
       }
     }
-    __syncthreads();  // chunk c's buffers are free for chunk c + 2
+    __syncthreads();  // chunk c's buffers are free for chunk c + VNB
   }
   if (active) {
     float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + j0;
@@ -487,14 +500,18 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
   if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
   if (!tiles && vec && hs % 2 == 0 && G * (hs / 2) <= 1024) {
     // one query token a tile: the decode kernels
-    attn_scores_decode<HALF, G><<<dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS,
-                                  (size_t)G * hs * sizeof(float), stream>>>(q, q_stride, kc, att, seq, pos, pos0,
+    const size_t smem_scores = (size_t)G * hs * sizeof(float) + (size_t)DEC_POS * (hs * (HALF ? 2 : 4) + 16);
+    if (smem_scores > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a key chunk");
+    B200_CUDA(cudaFuncSetAttribute(attn_scores_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)MAX_TILE_SMEM));
+    attn_scores_decode<HALF, G><<<dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS, smem_scores,
+                                  stream>>>(q, q_stride, kc, att, seq, pos, pos0,
                                                                             seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
     B200_LAUNCHED("attn_scores_decode");
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");
     const int threads = ((G * (hs / 2) + 31) / 32) * 32;
-    const size_t smem_values = (size_t)8 * VCH * hs + (size_t)8 * G * VCH;
+    const size_t smem_values = values_smem(hs, G, HALF);
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));

@@ -145,6 +145,17 @@ def cpu_sample(ckpt_host, plan, args, threads):
     return (args.cpu_prompt + args.cpu_gen) / dt, dt, setup
 
 
+def workload_config(args, world):
+    """the bench line's `config`, the same for both arms"""
+    S, P, G = args.seqs, args.prompt, args.gen
+    return {"workload": f"{args.model} int8 end to end: {S} sequences per GPU x ({P} prompt tokens prefilled in "
+                        f"blocks of {args.block} + {G} greedy tokens), sharded by sequence",
+            "model": args.model, "global_batch": S * world, "seq_len": P + G, "prompt": P, "generated": G,
+            "parallelism": f"dp{world} (independent sequences)", "kv": "float16",
+            "activations": "7-bit + bias 64 (relaxed)", "float_order": "exact (the reference's)",
+            "l2": "inputs larger than L2: 8.4 GB of weights read per step"}
+
+
 def reference_arm(args):
     """bench.py --impl reference: the oracle port of the reference's CPU path, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -172,7 +183,7 @@ def reference_arm(args):
     out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
-           "config": {"workload": f"{args.model} int8, {sample}", "model": args.model},
+           "config": workload_config(args, args.gpus),
            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference's AssemblyScript/WASM kernels cannot be built here (no node, no asc); the oracle "
@@ -319,12 +330,7 @@ def b200_arm(args):
             "metric": METRIC, "value": tokens / (ms_step / 1e3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{args.model} int8 end to end: {S} sequences per GPU x ({P} prompt tokens "
-                                   f"prefilled in blocks of {args.block} + {G} greedy tokens), sharded by sequence",
-                       "model": args.model, "global_batch": S * world, "seq_len": P + G, "prompt": P,
-                       "generated": G, "parallelism": f"dp{world} (independent sequences)", "kv": "float16",
-                       "activations": "7-bit + bias 64 (relaxed)", "float_order": "exact (the reference's)",
-                       "l2": "inputs larger than L2: 8.4 GB of weights read per step"},
+            "config": workload_config(args, world),
             "prefill_tok_s": S * (P - 1) * world / (pre / 1e3), "decode_tok_s": S * G * world / (dec / 1e3),
             "e2e": {"value": tokens / wall_step, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

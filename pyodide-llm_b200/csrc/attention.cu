@@ -370,12 +370,14 @@ __global__ void __launch_bounds__(DEC_POS)
 constexpr int VCH = 32;  // positions of a value chunk
 constexpr int VNB = 4;   // value chunks in flight (shared-memory buffers)
 
-// shared memory of attn_values_decode: VNB raw chunks, the widened chunk (float16 caches), VNB chunks of weights
-inline size_t values_smem(int hs, int G, bool half) {
-  return (size_t)VNB * VCH * hs * (half ? 2 : 4) + (half ? (size_t)VCH * hs * 4 : 0) + (size_t)VNB * G * VCH * 4;
+// shared memory of attn_values_decode for `dims` values of a head: VNB raw chunks, the widened chunk (float16
+// caches), VNB chunks of weights
+inline size_t values_smem(int dims, int G, bool half) {
+  return (size_t)VNB * VCH * dims * (half ? 2 : 4) + (half ? (size_t)VCH * dims * 4 : 0) + (size_t)VNB * G * VCH * 4;
 }
 
-// grid (kv heads, tokens), a thread two neighbouring values of one head (hs even): the same chain as
+// grid (kv heads, tokens, parts), part z of gridDim.z taking the head's values z * dims .. + dims (dims even); a
+// thread two neighbouring values of one head: the same chain as
 // attn_values_tiled, the positions in fours then one by one. The head's values come in chunks of VCH positions,
 // copied to shared memory asynchronously (cp.async, the next chunk on its way while this one is used), widened to
 // float32 once per block (the reference's half()), then read by the G heads' threads; the chunk's softmax weights
@@ -390,18 +392,19 @@ __global__ void __launch_bounds__(1024)
   extern __shared__ __align__(16) uint8_t vsm[];
   constexpr int ES = HALF ? 2 : 4;
   const int kvh = blockIdx.x, tok = blockIdx.y;
-  const int hp = hs / 2, hs4 = hs & ~3;
+  const int dims = hs / gridDim.z, dim0 = blockIdx.z * dims;  // this block's part of the head
+  const int hp = dims / 2, hs4 = hs & ~3;
   const int g = threadIdx.x / hp, jp = threadIdx.x % hp;
   const int h = kvh * G + g;
   const bool active = g < G && h >= h0 && h < h1;
   const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
   const int chunks = (count + VCH - 1) / VCH;
   const int64_t kvDim = (int64_t)nkv * hs;
-  const uint8_t *vbase =
-      reinterpret_cast<const uint8_t *>(vc) + ((seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs) * ES;
-  const int row_bytes = hs * ES, pieces = row_bytes / 16;
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(vc) +
+                         ((seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs + dim0) * ES;
+  const int row_bytes = dims * ES, pieces = row_bytes / 16;
   float *wide = reinterpret_cast<float *>(vsm + VNB * VCH * row_bytes);  // the chunk in float32 (HALF)
-  float *wts = reinterpret_cast<float *>(vsm + VNB * VCH * row_bytes + (HALF ? VCH * hs * 4 : 0));  // [VNB][G][VCH]
+  float *wts = reinterpret_cast<float *>(vsm + VNB * VCH * row_bytes + (HALF ? VCH * dims * 4 : 0));  // [VNB][G][VCH]
   const float *watt = att + ((int64_t)tok * nh + (int64_t)kvh * G) * P;  // head kvh * G + gg's row at gg * P
   // chunk c's values and weights into buffer c % VNB, one commit group per call (empty past the last chunk)
   auto issue = [&](int c) {
@@ -425,8 +428,8 @@ __global__ void __launch_bounds__(1024)
     }
     cp_async_commit();
   };
-  const int j0 = 2 * jp;
-  const bool fours = j0 < hs4;  // both of the thread's values lie in the head's fours (hs4 and j0 even)
+  const int j0 = 2 * jp;                // within the part; the head's value dim0 + j0
+  const bool fours = dim0 + j0 < hs4;   // both of the thread's values lie in the head's fours (hs4, dim0, j0 even)
   const uint64_t one2 = pk(one, one);
   uint64_t o = 0;  // the two values' sums
   for (int c = 0; c + 1 < VNB; c++) issue(c);
@@ -457,10 +460,10 @@ __global__ void __launch_bounds__(1024)
         if (p + 4 <= count4) {
           const float4 w4 = *reinterpret_cast<const float4 *>(w + i);
           const float w0 = w4.x, w1 = w4.y, w2 = w4.z, w3 = w4.w;
-          const uint64_t v0 = *reinterpret_cast<const uint64_t *>(vf + (i + 0) * hs + j0);
-          const uint64_t v1 = *reinterpret_cast<const uint64_t *>(vf + (i + 1) * hs + j0);
-          const uint64_t v2 = *reinterpret_cast<const uint64_t *>(vf + (i + 2) * hs + j0);
-          const uint64_t v3 = *reinterpret_cast<const uint64_t *>(vf + (i + 3) * hs + j0);
+          const uint64_t v0 = *reinterpret_cast<const uint64_t *>(vf + (i + 0) * dims + j0);
+          const uint64_t v1 = *reinterpret_cast<const uint64_t *>(vf + (i + 1) * dims + j0);
+          const uint64_t v2 = *reinterpret_cast<const uint64_t *>(vf + (i + 2) * dims + j0);
+          const uint64_t v3 = *reinterpret_cast<const uint64_t *>(vf + (i + 3) * dims + j0);
           if (fours) {
             const uint64_t s01 = fma2(one2, mul2(pk(w0, w0), v0), mul2(pk(w1, w1), v1));
             const uint64_t s23 = fma2(one2, mul2(pk(w2, w2), v2), mul2(pk(w3, w3), v3));
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(1024)
           // the positions past the fours, one at a time (kernel.ts:548-564)
           float a0 = lo(o), a1 = hi(o);
           for (int u = 0; u < 4 && p + u < count; u++) {
-            const float2 v = *reinterpret_cast<const float2 *>(vf + (i + u) * hs + j0);
+            const float2 v = *reinterpret_cast<const float2 *>(vf + (i + u) * dims + j0);
             a0 = fadd(a0, fmul(w[i + u], v.x));
             a1 = fadd(a1, fmul(w[i + u], v.y));
           }
@@ -485,7 +488,7 @@ __global__ void __launch_bounds__(1024)
     __syncthreads();  // chunk c's buffers are free for chunk c + VNB
   }
   if (active) {
-    float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + j0;
+    float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + dim0 + j0;
     dst[0] = lo(o);
     dst[1] = hi(o);
   }
@@ -510,12 +513,14 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     B200_LAUNCHED("attn_scores_decode");
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");
-    const int threads = ((G * (hs / 2) + 31) / 32) * 32;
-    const size_t smem_values = values_smem(hs, G, HALF);
+    // two parts of the head per token where each part's rows are whole 16-byte pieces: twice the blocks
+    const int parts = ((hs / 2) * (HALF ? 2 : 4)) % 16 == 0 && (hs / 2) % 2 == 0 ? 2 : 1;
+    const int threads = ((G * (hs / parts / 2) + 31) / 32) * 32;
+    const size_t smem_values = values_smem(hs / parts, G, HALF);
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));
-    attn_values_decode<HALF, G><<<dim3(nkv, count), threads, smem_values, stream>>>(
+    attn_values_decode<HALF, G><<<dim3(nkv, count, parts), threads, smem_values, stream>>>(
         out, out_stride, vc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
         P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0, 1.0f);
     B200_LAUNCHED("attn_values_decode");

@@ -14,6 +14,12 @@
 //           positions in fours ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) added in order, then the positions past the
 //           fours one by one (kernel.ts:522-565); values past the fours of a head add their four products one after
 //           another.
+//
+// Single query tokens (decode; the whole-head rows 16-byte aligned) take attn_scores_decode / attn_values_decode
+// instead: key chunks of DEC_POS positions and value chunks of VCH positions come to shared memory by cp.async
+// (the values VNB - 1 chunks ahead, with their softmax weights), are widened once per block, and the lane sums and
+// the fours of positions run on paired float32 operations (fma with a run-time one for the adds, so that every
+// product and sum keeps the reference's own rounding).
 #include <algorithm>
 #include <cfloat>
 #include <cstdint>

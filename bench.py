@@ -320,6 +320,9 @@ def b200_arm(args):
         roof = matmul_roofline(eng, S, peaks)
         roof["peak_source"] = which
         cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
+        # the same oracle on one thread, a shorter sample (4 prompt tokens + 2 greedy steps)
+        one = argparse.Namespace(**{**vars(args), "cpu_prompt": 4, "cpu_gen": 2})
+        cpu1_v, cpu1_dt, _ = cpu_sample(ckpt_host, plan, one, 1)
         del ckpt_host
         # each engine call copies its token table (4 x max_tokens int32) from pinned memory; greedy 2 more words
         runs = -(-(P - 1) // args.block)
@@ -338,6 +341,9 @@ def b200_arm(args):
             "cpu_baseline": {"value": cpu_v, "unit": "tok/s", "cores": host_threads(), "kind": "port",
                              "sample": f"1 sequence: {args.cpu_prompt} prompt tokens (one block) + {args.cpu_gen} "
                                        f"greedy steps of the same model ({cpu_dt:.1f} s)"},
+            "cpu_baseline_1thread": {"value": cpu1_v, "unit": "tok/s", "cores": 1, "kind": "port",
+                                     "sample": f"1 sequence: 4 prompt tokens (one block) + 2 greedy steps of the same "
+                                               f"model ({cpu1_dt:.1f} s)"},
             "gpu_launches": launches // max(1, args.steps) * args.steps,
             "clocks": clk,
         }

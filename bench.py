@@ -145,6 +145,25 @@ def cpu_sample(ckpt_host, plan, args, threads):
     return (args.cpu_prompt + args.cpu_gen) / dt, dt, setup
 
 
+def rank_prompts(seqs, prompt, vocab, rank):
+    """this rank's sequences of the workload (seeded by the rank: every rank its own, independent ones)"""
+    rng = np.random.default_rng(1000 + rank)
+    prompts = rng.integers(0, vocab, size=(seqs, prompt), dtype=np.int32)
+    prompts[:, 0] = BOS
+    return prompts
+
+
+def max_over_ranks(x, world, device):
+    """the largest of every rank's x (the job's time is its slowest rank's)"""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def workload_config(args, world):
     """the bench line's `config`, the same for both arms"""
     S, P, G = args.seqs, args.prompt, args.gen
@@ -241,9 +260,7 @@ def b200_arm(args):
                  max_tokens=S * args.block, capacity=P + G, device=local)
     del file
     torch.cuda.empty_cache()
-    rng = np.random.default_rng(1000 + rank)
-    prompts = rng.integers(0, vocab, size=(S, P), dtype=np.int32)
-    prompts[:, 0] = BOS
+    prompts = rank_prompts(S, P, vocab, rank)
     stream = eng.stream()
     st = torch.cuda.ExternalStream(stream)
     slots_all = np.arange(S, dtype=np.int32)
@@ -304,10 +321,7 @@ def b200_arm(args):
     launches = eng.launch_count() - launches0
 
     def worst(x):
-        t = torch.tensor([float(x)], device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return max_over_ranks(x, world, "cuda")
 
     ms_step = worst(np.mean(device_ms))
     wall_step = worst(np.mean(wall))

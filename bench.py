@@ -1,21 +1,24 @@
 #!/usr/bin/env python
-"""bench.py — decode+prefill tok/s of the int8 forward engine on the Llama-3-8B shape.
+"""bench.py — decode+prefill tok/s of the int8 forward engine: the Llama-3-8B shape, 64 sequences of 512 prompt tokens
++ 256 greedy tokens, sharded by sequence across 1/2/4/8 GPUs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config c5|c4]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-One step is one batch of the workload through the engine's C ABI: `seqs` sequences per GPU (64) of `prompt` (512)
-seeded random prompt tokens, prefilled in blocks (b200fwd_run), then `gen` (256) greedy tokens each on the device
-(b200fwd_generate_greedy). Weights: N(0, 0.02), quantized to int8 with one float32 scale per group of 32, made on the
-device (8.4 GB; far larger than L2, so every step reads them from HBM). Sequences are sharded across GPUs with no
-collective on the data path (each rank its own 64: weak scaling); ranks meet only at the timing barrier.
+One step is one batch of the workload through the engine's C ABI: `seqs` sequences in all (64) of `prompt` (512)
+seeded random prompt tokens, split evenly over the ranks; each rank prefills its sequences in blocks (b200fwd_run),
+then makes `gen` (256) greedy tokens each on the device (b200fwd_generate_greedy); then the ranks all-gather every
+sequence's generated ids (NCCL, the one collective on the data path). Weights: N(0, 0.02), quantized to int8 with one
+float32 scale per group of 32, made on the device and replicated on every GPU (8.4 GB; far larger than L2, so every
+step reads them from HBM). The total work is fixed as N grows (strong scaling).
 
-value: tokens (prompt + generated, all ranks) / the device time of the step's engine calls (CUDA events on the
-engine's stream, max over ranks). e2e: the same through the host-buffer calls, by the host clock around each step,
-host-to-device copies of the prompts and device-to-host reads of the generated ids inside. roofline: the dominant
-kernel (the int8 matmul) timed alone at the decode step's shapes with CUDA events, algorithmic bytes over its
-duration against the measured HBM copy bandwidth. cpu_baseline: the oracle (a C++ restatement of the reference's
-WASM-SIMD path, every host thread) on a bounded sample of the same workload.
+value: tokens processed (prompt positions 0..510 and the 256 greedy positions of every sequence) / the device time
+of the step (CUDA events around the engine's calls and the all-gather, max over ranks). e2e: the same through the
+host-buffer calls, by the host clock around each step, host-to-device copies of the prompts and device-to-host reads
+of the generated ids inside. roofline: the dominant kernel (the int8 matmul) timed alone at the decode step's shapes
+with CUDA events, algorithmic bytes over its duration against the measured HBM copy bandwidth. c4_matmul: the matmul
+alone at the 8B projection shapes at M = 1, 8, 64, 512 tokens. cpu_baseline: the oracle (a C++ restatement of the
+reference's WASM-SIMD path, built for the host's own CPU, every host thread) on a bounded sample of the workload.
 
 --impl reference: the reference's CPU path on this host (the oracle port: the reference's AssemblyScript kernels
 cannot be built or run here), every host thread, one sequence of the same model per step.
@@ -36,7 +39,7 @@ sys.path.insert(0, str(ROOT / "oracle"))
 
 import numpy as np  # noqa: E402
 
-METRIC = "decode+prefill tok/s, 8B-shape int8 (64 seq x (512 prompt + 256 greedy) per GPU)"
+METRIC = "decode+prefill tok/s, 8B-shape int8 (64 seq x (512 prompt + 256 greedy), sharded across the GPUs)"
 HEADER = (4096, 14336, 32, 32, 8, -128256, 8192)
 THETA = 500000.0
 BOS = 1
@@ -48,13 +51,16 @@ def parse():
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    p.add_argument("--seqs", type=int, default=64)
+    p.add_argument("--seqs", type=int, default=64, help="sequences in all (split evenly over the ranks)")
     p.add_argument("--prompt", type=int, default=512)
     p.add_argument("--gen", type=int, default=256)
     p.add_argument("--block", type=int, default=64, help="prompt positions per prefill call")
     p.add_argument("--cpu-prompt", type=int, default=16)
     p.add_argument("--cpu-gen", type=int, default=8)
     p.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "stories15m"])
+    p.add_argument("--config", default="c5", choices=["c5", "c4"],
+                   help="c5: the end-to-end line (default); c4: only the int8 matmul sweep over the 8B projection "
+                        "shapes at M = 1, 8, 64, 512 (also part of the c5 line)")
     p.add_argument("--matmul", default=None, metavar="ROWSxN",
                    help="time the int8 matmul alone (b200k_matmul_q8s) at ROWSxN with --seqs tokens, one matrix of "
                         "random weights on the device: the small case the kernel profiles are captured on")
@@ -65,6 +71,13 @@ def model_of(args):
     if args.model == "stories15m":
         return (288, 768, 6, 6, 6, 32000, 256), 10000.0
     return HEADER, THETA
+
+
+def cpu_model():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from build_oracle import cpu_model as model
+
+    return model()
 
 
 def host_threads():
@@ -129,6 +142,7 @@ def cpu_sample(ckpt_host, plan, args, threads):
     """The oracle on one sequence: cpu_prompt prompt tokens (one block) then cpu_gen greedy steps. tok/s."""
     import oracle
 
+    oracle.use_native()
     t0 = time.perf_counter()
     eng = oracle.OracleEngine(ckpt_host, plan, half_keys=1, threads=threads)
     setup = time.perf_counter() - t0
@@ -145,12 +159,35 @@ def cpu_sample(ckpt_host, plan, args, threads):
     return (args.cpu_prompt + args.cpu_gen) / dt, dt, setup
 
 
-def rank_prompts(seqs, prompt, vocab, rank):
-    """this rank's sequences of the workload (seeded by the rank: every rank its own, independent ones)"""
-    rng = np.random.default_rng(1000 + rank)
+def workload_prompts(seqs, prompt, vocab):
+    """every sequence's prompt (seeded: the same workload at every GPU count), each starting with BOS"""
+    rng = np.random.default_rng(1000)
     prompts = rng.integers(0, vocab, size=(seqs, prompt), dtype=np.int32)
     prompts[:, 0] = BOS
     return prompts
+
+
+def shard(seqs, world, rank):
+    """the sequences rank `rank` of `world` takes: an even split (every rank the same count, so that the all-gather
+    of the generated ids has equal parts)"""
+    if seqs % world:
+        raise SystemExit(f"{seqs} sequences do not split evenly over {world} GPUs")
+    per = seqs // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+def gather_ids(ids, world, device):
+    """every rank's generated ids [per rank][steps] gathered on every rank in rank order [seqs][steps] (NCCL
+    all-gather over NVLink; the one collective on the data path). Returns the gathered device tensor."""
+    import torch
+    import torch.distributed as dist
+
+    local = torch.from_numpy(np.ascontiguousarray(ids, np.int32)).to(device, non_blocking=True)
+    if world == 1:
+        return local
+    out = torch.empty((world * local.shape[0], local.shape[1]), dtype=torch.int32, device=device)
+    dist.all_gather_into_tensor(out, local)
+    return out
 
 
 def max_over_ranks(x, world, device):
@@ -167,10 +204,12 @@ def max_over_ranks(x, world, device):
 def workload_config(args, world):
     """the bench line's `config`, the same for both arms"""
     S, P, G = args.seqs, args.prompt, args.gen
-    return {"workload": f"{args.model} int8 end to end: {S} sequences per GPU x ({P} prompt tokens prefilled in "
-                        f"blocks of {args.block} + {G} greedy tokens), sharded by sequence",
-            "model": args.model, "global_batch": S * world, "seq_len": P + G, "prompt": P, "generated": G,
-            "parallelism": f"dp{world} (independent sequences)", "kv": "float16",
+    return {"workload": f"{args.model} int8 end to end: {S} sequences x ({P} prompt tokens prefilled in blocks of "
+                        f"{args.block} positions + {G} greedy tokens), sharded by sequence over {world} GPU(s), "
+                        f"the generated ids all-gathered",
+            "model": args.model, "global_batch": S, "seq_len": P + G, "prompt": P, "generated": G,
+            "tokens_per_sequence": P - 1 + G,
+            "parallelism": f"dp{world} (independent sequences, weights replicated)", "kv": "float16",
             "activations": "7-bit + bias 64 (relaxed)", "float_order": "exact (the reference's)",
             "l2": "inputs larger than L2: 8.4 GB of weights read per step"}
 
@@ -200,10 +239,11 @@ def reference_arm(args):
     sample = (f"1 sequence per step: {args.cpu_prompt} prompt tokens in one block + {args.cpu_gen} greedy steps, "
               f"the whole {args.model} int8 model")
     out = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+           "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
            "config": workload_config(args, args.gpus),
-           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
+                            "cpu": cpu_model(), "build": "g++ -O3 -march=native -ffp-contract=off"},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference's AssemblyScript/WASM kernels cannot be built here (no node, no asc); the oracle "
                    "is their C++ restatement, pinned to the reference's bit-exact checks"}
@@ -234,6 +274,65 @@ def matmul_roofline(eng, M, peaks, reps=3):
             "algorithmic_bytes_per_launch": per_launch_bytes, "pass_ms": ms}
 
 
+C4_SHAPES = {"qkv": "6144x4096", "o": "4096x4096", "w13": "28672x4096", "w2": "4096x14336"}
+
+
+def c4_sweep(eng, peaks, counts=(1, 8, 64, 512), reps=2):
+    """The int8 matmul at the 8B projection shapes (q|k|v 6144x4096, o 4096x4096, w1|w3 28672x4096, w2 4096x14336)
+    at M tokens, each shape over all 32 layers' copies in turn so that no launch finds its weights in L2
+    (b200fwd_time_matmul_kinds), on the engine's activations. M <= 64: HBM-bound (bytes = rows n 9/8 + M n 9/8 +
+    4 M rows); M = 512: ops = 2 M rows n against twice the measured bf16 tensor rate (the int8 rate), and the exact
+    epilogue's CUDA-core floor (3 float32 operations per row, token and group of 32 at 128 lanes x SM clock)."""
+    hbm = float(peaks["hbm_gbs"])
+    int8_tops = 2.0 * float(peaks["bf16_tflops"])
+    sm_hz = float(peaks.get("sm_max_mhz", 1965.0)) * 1e6
+    out = {}
+    for m in counts:
+        kinds = eng.time_matmul_kinds(m, reps)
+        row = {}
+        for k, shape in C4_SHAPES.items():
+            us, nbytes = kinds[k]
+            rows, n = (int(v) for v in shape.split("x"))
+            gbs = nbytes / (us * 1e-6) / 1e9
+            e = {"us": round(us, 2), "gb_s": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4)}
+            if m >= 512:
+                tops = 2.0 * m * rows * n / (us * 1e-6) / 1e12
+                floor_us = 3.0 * m * rows * (n // 32) / (148 * 128 * sm_hz) * 1e6
+                e.update({"tops": round(tops, 1), "int8_tensor_frac": round(tops / int8_tops, 4),
+                          "fp32_epilogue_floor_us": round(floor_us, 2)})
+            row[shape] = e
+        out[f"M={m}"] = row
+    return {"what": "int8 group-32 matmul (exact order) per launch, every layer's copy in turn (no L2 hits)",
+            "kernel": "matvec_kernel (CUDA cores) below 16 tokens, q8_gemm_tc (tcgen05) from 16",
+            "peak_hbm_gbs": hbm, "int8_tops_peak": int8_tops, "table": out}
+
+
+def c4_arm(args):
+    """bench.py --config c4: the matmul sweep alone on the 8B-shape engine (one GPU)."""
+    import torch
+
+    from b200fwd import synthetic
+    from b200fwd.forward import Engine
+
+    torch.cuda.set_device(0)
+    header, theta = model_of(args)
+    file = synthetic.make(header, seed=0, device="cuda")
+    plan = synthetic.plan_for(header, file, theta)
+    eng = Engine(file.data_ptr(), plan, checkpoint_on_device=True, size=file.numel(), half_keys=True, slots=1,
+                 max_tokens=512, capacity=512)
+    del file
+    torch.cuda.empty_cache()
+    rng = np.random.default_rng(3)
+    tokens = rng.integers(0, abs(header[5]), 512).astype(np.int32)
+    eng.run(np.zeros(512, np.int32), tokens, np.arange(512, dtype=np.int32))  # activations of a real block
+    peaks, which = measured_peaks()
+    res = c4_sweep(eng, peaks)
+    res["peak_source"] = which
+    print(json.dumps({"config": "c4", **res}), flush=True)
+    eng.release()
+    return 0
+
+
 def b200_arm(args):
     import ctypes
 
@@ -252,7 +351,8 @@ def b200_arm(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     header, theta = model_of(args)
     vocab = abs(header[5])
-    S, P, G = args.seqs, args.prompt, args.gen
+    mine = shard(args.seqs, world, rank)
+    S, P, G = mine.stop - mine.start, args.prompt, args.gen
     file = synthetic.make(header, seed=0, device="cuda")
     plan = synthetic.plan_for(header, file, theta)
     ckpt_host = file.cpu().numpy() if rank == 0 else None
@@ -260,7 +360,7 @@ def b200_arm(args):
                  max_tokens=S * args.block, capacity=P + G, device=local)
     del file
     torch.cuda.empty_cache()
-    prompts = rank_prompts(S, P, vocab, rank)
+    prompts = workload_prompts(args.seqs, P, vocab)[mine]
     stream = eng.stream()
     st = torch.cuda.ExternalStream(stream)
     slots_all = np.arange(S, dtype=np.int32)
@@ -290,7 +390,13 @@ def b200_arm(args):
         if events is not None:
             events.append(torch.cuda.Event(enable_timing=True))
             events[-1].record(st)
-        return ids
+            events.append(torch.cuda.Event(enable_timing=True))
+            events[-1].record()
+        every = gather_ids(ids, world, "cuda")
+        if events is not None:
+            events.append(torch.cuda.Event(enable_timing=True))
+            events[-1].record()
+        return every.cpu().numpy() if rank == 0 else None
 
     for _ in range(args.warmup):
         step()
@@ -303,7 +409,7 @@ def b200_arm(args):
 
     barrier()
     launches0 = eng.launch_count()
-    wall, device_ms, prefill_ms, decode_ms = [], [], [], []
+    wall, device_ms, prefill_ms, decode_ms, gather_ms = [], [], [], [], []
     torch.cuda.nvtx.range_push("timed")  # lets a profiler keep to the timed steps (ncu --nvtx-include timed/)
     with Clocks(local) as clocks:
         for _ in range(args.steps):
@@ -313,8 +419,9 @@ def b200_arm(args):
             torch.cuda.synchronize()
             wall.append(time.perf_counter() - t0)
             pairs = [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)]
-            prefill_ms.append(sum(pairs[:-1]))
-            decode_ms.append(pairs[-1])
+            prefill_ms.append(sum(pairs[:-2]))
+            decode_ms.append(pairs[-2])
+            gather_ms.append(pairs[-1])
             device_ms.append(sum(pairs))
     torch.cuda.nvtx.range_pop()
     barrier()
@@ -327,37 +434,44 @@ def b200_arm(args):
     wall_step = worst(np.mean(wall))
     pre = worst(np.mean(prefill_ms))
     dec = worst(np.mean(decode_ms))
-    tokens = S * (P + G) * world
+    gat = worst(np.mean(gather_ms))
+    tokens = args.seqs * (P - 1 + G)
     result = None
     if rank == 0:
         peaks, which = measured_peaks()
         roof = matmul_roofline(eng, S, peaks)
         roof["peak_source"] = which
+        c4 = c4_sweep(eng, peaks)
         cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
         # the same oracle on one thread, a shorter sample (4 prompt tokens + 2 greedy steps)
         one = argparse.Namespace(**{**vars(args), "cpu_prompt": 4, "cpu_gen": 2})
         cpu1_v, cpu1_dt, _ = cpu_sample(ckpt_host, plan, one, 1)
         del ckpt_host
-        # each engine call copies its token table (4 x max_tokens int32) from pinned memory; greedy 2 more words
+        # each engine call copies its token table (4 x max_tokens int32) from pinned memory; greedy 2 more words;
+        # the generated ids go to the device for the all-gather
         runs = -(-(P - 1) // args.block)
-        h2d = (runs + 1) * 16 * S * args.block + 8
-        d2h = S * G * 4 + 4  # the generated ids and the not-finite flag
+        h2d = (runs + 1) * 16 * S * args.block + 8 + S * G * 4
+        d2h = S * G * 4 + 4 + args.seqs * G * 4  # the ids and the not-finite flag; rank 0 reads every sequence's ids
         clk = clocks.summary()
         result = {
             "metric": METRIC, "value": tokens / (ms_step / 1e3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": workload_config(args, world),
-            "prefill_tok_s": S * (P - 1) * world / (pre / 1e3), "decode_tok_s": S * G * world / (dec / 1e3),
+            "prefill_tok_s": args.seqs * (P - 1) / (pre / 1e3), "decode_tok_s": args.seqs * G / (dec / 1e3),
+            "gather_ms": gat, "per_gpu_sequences": S,
             "e2e": {"value": tokens / wall_step, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": roof,
             "cpu_baseline": {"value": cpu_v, "unit": "tok/s", "cores": host_threads(), "kind": "port",
                              "sample": f"1 sequence: {args.cpu_prompt} prompt tokens (one block) + {args.cpu_gen} "
-                                       f"greedy steps of the same model ({cpu_dt:.1f} s)"},
+                                       f"greedy steps of the same model ({cpu_dt:.1f} s); the reference's CPU path "
+                                       f"holds one sequence, so this is unbatched against the GPU's 64",
+                             "cpu": cpu_model(), "build": "g++ -O3 -march=native -ffp-contract=off"},
             "cpu_baseline_1thread": {"value": cpu1_v, "unit": "tok/s", "cores": 1, "kind": "port",
                                      "sample": f"1 sequence: 4 prompt tokens (one block) + 2 greedy steps of the same "
                                                f"model ({cpu1_dt:.1f} s)"},
+            "c4_matmul": c4,
             "gpu_launches": launches // max(1, args.steps) * args.steps,
             "clocks": clk,
         }
@@ -420,6 +534,8 @@ def main():
         return reference_arm(args)
     if args.matmul:
         return matmul_arm(args)
+    if args.config == "c4":
+        return c4_arm(args)
     return b200_arm(args)
 
 

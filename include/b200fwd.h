@@ -156,6 +156,15 @@ int b200fwd_launch_count(b200fwd_engine *engine, uint64_t *out);
 int b200fwd_time_matmuls(b200fwd_engine *engine, int32_t count, int32_t reps, float *ms_per_pass,
                          double *bytes_per_pass, int32_t *launches_per_pass);
 
+/* No counterpart in the reference: a measurement aid. The int8 matmul of each weight-matrix kind at `count` tokens,
+ * as the forward pass launches it: [0] q|k|v (qDim + 2 kvDim rows), [1] o (dim rows), [2] w1|w3 (2 hidden rows),
+ * [3] w2 (dim rows, n = hidden), [4] the classifier (vocab rows). Each kind runs over every layer's copy in turn (so
+ * no launch finds its weights in L2), one warm-up pass then `reps` timed passes, CUDA events on the engine's stream.
+ * Gives the average GPU time of one launch of each kind (microseconds) and its algorithmic bytes (weights + scales
+ * + activations read once, outputs written once). The engine's state is left as it was. */
+int b200fwd_time_matmul_kinds(b200fwd_engine *engine, int32_t count, int32_t reps, float *us_per_launch,
+                              double *bytes_per_launch);
+
 /* ---------------------------------------------------------------------------------------------- the kernels
  * Device pointers, a stream, and the reference's arguments. `count` tokens of a prompt (T108) sit `*_stride`
  * elements apart where the reference keeps them a frame apart. Return 0 or B200FWD_E*. */

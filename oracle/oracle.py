@@ -18,6 +18,16 @@ sys.path.insert(0, str(HERE.parent / "pyodide-llm_b200"))
 from b200fwd.abi import Plan, plan_struct  # noqa: E402
 
 _lib = None
+_native = False
+
+
+def use_native():
+    """Load the oracle built on and for this host's CPU (-march=native; built now, before the first call): the
+    timed CPU baseline. Same numbers as the portable build."""
+    global _native
+    if _lib is not None and not _native:
+        raise RuntimeError("the portable oracle is already loaded in this process")
+    _native = True
 
 
 def load():
@@ -26,7 +36,7 @@ def load():
         sys.path.insert(0, str(HERE))
         from build_oracle import build
 
-        path = build()
+        path = build(native=_native)
         lib = ctypes.CDLL(str(path))
         P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
         sigs = {

@@ -142,6 +142,7 @@ def load():
         "b200fwd_launch_count": (P, ctypes.POINTER(U64)),
         "b200fwd_time_matmuls": (P, I32, I32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double),
                                  ctypes.POINTER(I32)),
+        "b200fwd_time_matmul_kinds": (P, I32, I32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)),
         "b200k_quantize_x": (P, P, P, I32, I32, I32, I64, I64, I64, P),
         "b200k_int8_sums": (P, P, I64, P),
         "b200k_matmul_q8r": (P, P, P, P, P, P, I32, I32, I32, I32, I64, I64, I64, P),

@@ -151,6 +151,15 @@ class Engine:
                                                  ctypes.byref(launches)), "time_matmuls")
         return ms.value, nbytes.value, launches.value
 
+    KINDS = ("qkv", "o", "w13", "w2", "classifier")
+
+    def time_matmul_kinds(self, count, reps=3):
+        """{kind: (us per launch, algorithmic bytes per launch)} of each weight-matrix kind at `count` tokens, every
+        layer's copy in turn (b200fwd_time_matmul_kinds)."""
+        us, nbytes = (ctypes.c_float * 5)(), (ctypes.c_double * 5)()
+        abi.check(self._lib.b200fwd_time_matmul_kinds(self._h, count, reps, us, nbytes), "time_matmul_kinds")
+        return {k: (us[i], nbytes[i]) for i, k in enumerate(self.KINDS)}
+
     def stream(self):
         out = ctypes.c_void_p()
         abi.check(self._lib.b200fwd_stream_of(self._h, ctypes.byref(out)), "stream")

@@ -91,9 +91,9 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     }
     int *err = nullptr;
     B200_CUDA(cudaGetSymbolAddress((void **)&err, capi_tc_error));
-    const int row_tiles = (rows + 127) / 128;
-    int bn = 32;
-    while (bn > 16 && (bn > count || row_tiles * ((count + bn - 1) / bn) < 148)) bn /= 2;
+    const int sms = gemm_sms();
+    if (sms < 0) return sms;
+    const int bn = choose_gemm_bn(rows, count, sms, 64);
     // the kernel reads the activation scales one row per group: a stream-ordered copy in that layout
     const int64_t tstride = (count + 3) / 4 * 4;
     float *xs_g = nullptr;

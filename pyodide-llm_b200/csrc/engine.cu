@@ -100,8 +100,10 @@ struct b200fwd_engine {
   int logit_rows = 0;
   int32_t *argmax = nullptr;
   int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tc error, -, tiles[2T]
-  CUtensorMap xmap[2], xsmap[2]; // the activations and their scales, for tiles of 16 and 32 tokens
+  CUtensorMap xmap[3], xsmap[3]; // the activations and their scales, for tiles of 16, 32 and 64 tokens
+  int widest_tile = 0;           // the widest of those tiles the activations have room for
   bool tensor_cores = true;
+  int sms = 148;
   int32_t *meta_h = nullptr;    // pinned host copy
   int32_t *history = nullptr;   // greedy ids [slots][steps]
   int history_len = 0;
@@ -256,13 +258,13 @@ int alloc_activations(b200fwd_engine *e) {
   B200_CUDA(cudaMemsetAsync(e->meta, 0, (size_t)(6 * T + 4) * 4, e->stream));
   B200_CUDA(cudaMallocHost((void **)&e->meta_h, (size_t)(6 * T + 4) * 4));
   // the activations' TMA maps (rows of XQ bytes, one per token) and their scales' (rows of TP floats, one per group),
-  // for tiles of 16 and 32 tokens
-  const int bns[2] = {16, 32};
+  // for tiles of 16, 32 and 64 tokens (as many as T holds)
   e->tensor_cores = e->tensor_cores && T >= 32 && e->XQ >= 128;
   if (e->tensor_cores)
-    for (int i = 0; i < 2; i++) {
-      CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bns[i]));
-      CHECK(make_token_scale_map(&e->xsmap[i], e->xs, T, e->XQ / 32, e->TP, bns[i]));
+    for (int i = 0, bn = 16; i < 3 && bn <= T; i++, bn *= 2) {
+      CHECK(make_i8_map(&e->xmap[i], e->xq, e->XQ, T, e->XQ, bn));
+      CHECK(make_token_scale_map(&e->xsmap[i], e->xs, T, e->XQ / 32, e->TP, bn));
+      e->widest_tile = bn;
     }
   return 0;
 }
@@ -302,10 +304,12 @@ int grow(b200fwd_engine *e, int pos) {
 }
 
 // one matrix of one layer times the quantized activations of count tokens (in e->xq, less the bias): the tensor
-// cores from 16 tokens on (gemm_tc.cu), the CUDA cores below (kernels.cu); the same numbers either way
+// cores from TC_MIN_TOKENS tokens on (gemm_tc.cu; a tile of 16 token columns whose columns past count read rows of the
+// activation buffer that no output uses), the CUDA cores for one token (kernels.cu); the same numbers either way
+constexpr int TC_MIN_TOKENS = 2;
 int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t out_stride, int accumulate, int count) {
-  // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 32 tokens: never past the tensors' extents)
-  if (count >= 16 && e->relaxed && e->tensor_cores && m.mapped) {
+  // (the TMA boxes are 128 bytes of K by 128 weight rows and by up to 64 tokens: never past the tensors' extents)
+  if (count >= TC_MIN_TOKENS && e->relaxed && e->tensor_cores && m.mapped) {
     GemmArgs a{};
     a.out = out;
     a.error = e->tc_error_d();
@@ -315,11 +319,8 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
     a.w_row0 = layer * m.rows;
     a.out_stride = out_stride;
     a.accumulate = accumulate;
-    // tiles of 32 tokens unless they would leave more than half the SMs idle (measured at 64 tokens: 6144 rows
-    // run faster as 96 wide tiles than as 192 narrow ones, 4096 rows slower as 64 wide tiles than as 128 narrow)
-    const int row_tiles = (m.rows + 127) / 128;
-    const int bn = count >= 32 && row_tiles * ((count + 31) / 32) >= 74 ? 32 : 16;
-    const int which = bn == 16 ? 0 : 1;
+    const int bn = choose_gemm_bn(m.rows, count, e->sms, e->widest_tile);
+    const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
     GemmMaps maps{m.wmap, e->xmap[which], m.smap, e->xsmap[which]};
     return launch_gemm_tc(maps, a, bn, e->stream);
   }
@@ -479,6 +480,8 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
   B200_CUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   CHECK(prepare_attention());
   CHECK(prepare_gemm());
+  e->sms = gemm_sms();
+  if (e->sms <= 0) return fail(B200FWD_ECUDA, "no SM count");
   const uint8_t *ck = (const uint8_t *)checkpoint;
   const bool dev = opt.checkpoint_on_device != 0;
   CHECK(upload_matrix(e, ck, size, dev, p.token_embedding_table, "token_embedding_table", e->emb));
@@ -767,6 +770,56 @@ int b200fwd_time_matmuls(b200fwd_engine *e, int32_t count, int32_t reps, float *
     *bytes_per_pass = total;
     *launches_per_pass = 4 * e->layers + 1;
     return 0;
+  });
+}
+
+int b200fwd_time_matmul_kinds(b200fwd_engine *e, int32_t count, int32_t reps, float *us_per_launch,
+                              double *bytes_per_launch) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    if (count < 1 || count > e->T || reps < 1 || !us_per_launch || !bytes_per_launch)
+      return fail(B200FWD_EINVAL, "time_matmul_kinds: bad arguments");
+    const Matrix *mats[5] = {&e->wqkv, &e->wo, &e->w13, &e->w2, &e->wcls};
+    int most = 0;
+    for (const Matrix *m : mats) most = std::max(most, m->rows);
+    float *out = nullptr;
+    B200_CUDA(cudaMallocAsync((void **)&out, (size_t)count * most * 4, e->stream));
+    struct Free {
+      float *p;
+      cudaStream_t s;
+      ~Free() { cudaFreeAsync(p, s); }
+    } free_out{out, e->stream};
+    cudaEvent_t t0, t1;
+    B200_CUDA(cudaEventCreate(&t0));
+    B200_CUDA(cudaEventCreate(&t1));
+    struct Drop {
+      cudaEvent_t a, b;
+      ~Drop() {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+      }
+    } drop{t0, t1};
+    for (int k = 0; k < 5; k++) {
+      const Matrix &m = *mats[k];
+      const int layers = k == 4 ? 1 : e->layers;
+      // every layer's copy of the matrix in turn (distinct memory: a layer's weights are out of L2 again by the time
+      // its turn comes back); the classifier alone is larger than L2
+      auto pass = [&]() -> int {
+        for (int l = 0; l < layers; l++) CHECK(matmul(e, m, l, out, m.rows, 0, count));
+        return 0;
+      };
+      CHECK(pass());  // warm-up
+      B200_CUDA(cudaEventRecord(t0, e->stream));
+      for (int r = 0; r < reps; r++) CHECK(pass());
+      B200_CUDA(cudaEventRecord(t1, e->stream));
+      B200_CUDA(cudaEventSynchronize(t1));
+      float ms = 0;
+      B200_CUDA(cudaEventElapsedTime(&ms, t0, t1));
+      us_per_launch[k] = ms * 1000.0f / (float)(reps * layers);
+      bytes_per_launch[k] =
+          (double)m.rows * m.n * (1.0 + 4.0 / 32) + (double)count * m.n * (1.0 + 4.0 / 32) + 4.0 * count * m.rows;
+    }
+    return check_tc(e);
   });
 }
 

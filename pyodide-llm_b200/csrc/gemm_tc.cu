@@ -1,21 +1,28 @@
 // gemm_tc.cu — the int8 group-32 matmul of a prompt block or of many sequences' tokens on the 5th-generation tensor
-// cores: kernel_relaxed.ts:34-67 / 164-183 (matmul_q8r, matmul_q8r_tile) for count >= 16 tokens, to the bit.
+// cores: kernel_relaxed.ts:34-67 / 164-183 (matmul_q8r, matmul_q8r_tile) for two tokens and more, to the bit.
 //
 // The reference's number for (row r, token t) is a float chain over the row's groups of 32: each group's exact
-// integer dot(w, q - 64) times (weight scale x activation scale), rounded once, added into lane g % 4 for the groups
-// below the last four, the lanes added ((0 + 1) + 2) + 3, then the groups past the fours one at a time. Here:
+// integer dot(w, q - 64), as float32, times (weight scale x activation scale), rounded once, added into lane g % 4
+// for the groups below the last four, the lanes added ((0 + 1) + 2) + 3, then the groups past the fours one at a
+// time. Here, in a persistent kernel (one block per SM walking tiles of 128 weight rows x BN tokens):
 //   - warp 0: TMA brings 128 weight rows x 128 bytes (four groups), BN tokens' activations x 128 bytes and both
-//     scale tiles per stage into shared memory, 8 stages deep (128-byte swizzle; no multicast);
-//   - warp 1: one thread issues one tcgen05.mma kind::i8 per group (K = 32: exactly one group) into a TMEM column
-//     block of its own (128 lanes = rows, BN columns = tokens): every group's int32 sums, exact, none added to
-//     another. TMEM holds several stages at once (slots), and one tcgen05.commit per stage releases a slot;
-//   - warps 2..17 (epilogue): four per TMEM lane quarter, each with BN / 4 tokens, read their groups' sums
+//     scale tiles per stage into shared memory, several stages deep (128-byte swizzle; no multicast);
+//   - warp 1: one thread issues, per stage, into a TMEM slot of four column blocks (128 lanes = rows, BN columns =
+//     tokens, one block per group): a kind::f16 MMA whose constant operands (512 x 1536, sixteen times) write
+//     1.5 * 2^23 into all four blocks; one kind::i8 MMA per group (K = 32: exactly one group) that adds the
+//     group's int32 sums to those words as integers, giving the bit patterns of the floats 1.5 * 2^23 + S; and a
+//     second kind::f16 MMA (512 x -1536) that takes 1.5 * 2^23 off again in float32. Every step is exact (integers
+//     below 2^24 throughout), so TMEM ends up holding float(S) of every (row, token, group), none added to another;
+//   - warps 4..19 (epilogue): four per TMEM lane quarter, each with BN / 4 tokens, read their groups' floats
 //     (tcgen05.ld) and keep the reference's four chain accumulators of each (row, token) in registers, with one
-//     rounding per float operation (__fmul_rn / __fadd_rn; no contraction, built with --fmad=false).
+//     rounding per float operation (__fmul_rn / __fadd_rn, built with --fmad=false): per (row, token, group) a
+//     scale product, a product and a chain add.
 // Every mbarrier wait has an iteration limit: past it the kernel records an error and returns (no hang).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -28,12 +35,17 @@ namespace {
 
 constexpr int BM = 128;                 // rows of a tile (TMEM lanes)
 constexpr int KSTAGE = 128;             // bytes of K per stage: four groups
-constexpr int STAGES = 8;
-constexpr int BN_MAX = 32;            // tokens of a tile at most (32 accumulators a thread)
 constexpr int EPI_WARPS = 16;
-constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int EPI_WARP0 = 4;  // warps 0..3 (one warpgroup): the producer, the MMA issuer and two idle warps
+constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+// registers per thread: THREADS x 96 at launch; the first warpgroup gives back all but 32 a thread and the four
+// epilogue warpgroups take 112 (128 x 32 + 512 x 112 = 640 x 96: the launch's whole share)
+constexpr int REGS_SMALL = 32, REGS_EPILOGUE = 112;
 constexpr uint32_t WAIT_HINT_NS = 1000000;  // 1 ms
 constexpr uint32_t WAIT_TRIES = 2000;
+
+// f16 bit patterns of the constant operands of the offset MMAs: 16 x 512 x 1536 = 12582912 = 1.5 * 2^23
+constexpr uint32_t F16_512 = 0x6000u, F16_1536 = 0x6600u, F16_MINUS_1536 = 0xE600u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -93,21 +105,45 @@ __device__ __forceinline__ uint64_t smem_desc(const void *p) {
   return d;
 }
 
-// instruction descriptor: kind::i8, D int32, A and B signed int8, both K-major, M = 128, N = bn
-__host__ __device__ constexpr uint32_t idesc_i8(int bn) {
-  return (2u << 4)                         // D format: S32
-         | (1u << 7) | (1u << 10)          // A, B: signed 8-bit
-         | ((uint32_t)(bn >> 3) << 17)     // N >> 3
-         | ((uint32_t)(BM >> 4) << 24);    // M >> 4
+// descriptor of a constant operand (every element the same value): K-major, no swizzle, 8 x 16-byte core matrices
+// 128 bytes apart along K and 256 bytes apart along M/N. (Whatever order the hardware walks them in, it reads
+// inside the buffer and sees the one value.)
+__device__ __forceinline__ uint64_t const_desc(const void *p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3fff;
+  d |= (uint64_t)(128 >> 4) << 16;
+  d |= (uint64_t)(256 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
 }
 
-// D = A x B (each group's MMA writes its own column block)
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+// instruction descriptor: kind::i8, D int32, A and B signed int8, both K-major, M = 128, N = n
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4)                         // D format: S32
+         | (1u << 7) | (1u << 10)          // A, B: signed 8-bit
+         | ((uint32_t)(n >> 3) << 17)      // N >> 3
+         | ((uint32_t)(BM >> 4) << 24);    // M >> 4
+}
+// instruction descriptor: kind::f16, D float32, A and B float16, both K-major, M = 128, N = n
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 0, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -119,50 +155,55 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Two float32 lanes at once (PTX .f32x2), each lane rounded on its own. A paired multiply whose product feeds a
-// paired add is fused into one fma below PTX (one rounding: not the reference's number); a product that is the addend
-// of an fma cannot be fused. So the chains add as fma(one, acc, product), `one` being 1.0f from a kernel argument:
-// acc * 1 is exact, and acc + product is then rounded once, as an add rounds it.
-__device__ __forceinline__ uint64_t pack2(uint32_t a, uint32_t b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+template <int BN>
+struct Tile {
+  static constexpr int STAGES = BN == 64 ? 7 : 8;
+  static constexpr int SLOTS = 512 / (4 * BN);  // TMEM holds this many stages' four groups at once
+  static constexpr int TPW = BN / 4;            // tokens of an epilogue warp
+  static constexpr int GB = BN == 64 ? 1 : 4;   // groups whose sums an epilogue warp loads from TMEM at once
+};
 
-// an int32 below 2^22 in magnitude as float32, exactly: its bits added to those of 1.5 * 2^23, less 1.5 * 2^23
-constexpr uint32_t MAGIC_BITS = 0x4B400000u;
-constexpr float MAGIC = 12582912.0f;
+// a position in a ring of N buffers and the parity of its current round (advanced by one at a time: no division)
+template <int N>
+struct Ring {
+  int i = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++i == N) {
+      i = 0;
+      phase ^= 1;
+    }
+  }
+};
 
+template <int BN>
 struct Smem {
+  static constexpr int STAGES = Tile<BN>::STAGES;
   alignas(1024) uint8_t a[STAGES][BM * KSTAGE];       // 128 weight rows x four groups
-  alignas(1024) uint8_t b[STAGES][BN_MAX * KSTAGE];   // the tokens x four groups
+  alignas(1024) uint8_t b[STAGES][BN * KSTAGE];       // the tokens x four groups
   alignas(128) float ws[STAGES][BM][4];               // the rows' four groups' scales
-  alignas(128) float xs[STAGES][4 * BN_MAX];          // the tokens' scales: four rows (groups) of bn tokens
+  alignas(128) float xs[STAGES][4 * BN];              // the tokens' scales: four rows (groups) of BN tokens
+  alignas(128) uint16_t ka[BM * 16];                  // the offset MMAs' constant operands (float16)
+  alignas(128) uint16_t kb_plus[4 * BN * 16];
+  alignas(128) uint16_t kb_minus[4 * BN * 16];
   uint64_t full[STAGES], empty[STAGES];
-  uint64_t slot_full[8], slot_empty[8];  // TMEM stage slots: four groups' columns each
+  uint64_t slot_full[Tile<BN>::SLOTS], slot_empty[Tile<BN>::SLOTS];
+  uint64_t mma_done;
   uint32_t tmem_base;
 };
 
 // TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes
 template <int TPW>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[TPW]);
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -176,24 +217,33 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
-// Warp roles: 0 TMA producer, 1 MMA issue, 2..17 epilogue. Epilogue warp w reads TMEM lane quarter w % 4 (its 32
-// rows) and token columns (w - 2) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
-// its (row, token) in registers, two tokens to a 64-bit pair: the chains, their sum and the groups past the fours
-// all happen in one thread. A group's sum S becomes float(S) as (the float with bits S + magic_bits) - magic.
-template <int BN>
+// Warp roles: 0 TMA producer, 1 MMA issue, 2 and 3 idle, 4..19 epilogue. Epilogue warp w reads TMEM lane quarter
+// w % 4 (its 32 rows) and token columns (w - 4) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
+// its (row, token) in registers: the chains, their sum and the groups past the fours all happen in one thread. Tiles go round the blocks (tile = block, block + grid, ...): consecutive tiles share
+// their weight rows, so blocks that run together read each weight row once from HBM.
+// TAIL: n / 32 is not a multiple of four (groups past the fours); without it every stage is four whole groups
+template <int BN, bool TAIL>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap, GemmArgs args) {
+  using T = Tile<BN>;
+  constexpr int STAGES = T::STAGES, SLOTS = T::SLOTS, TPW = T::TPW, GB = T::GB;
   extern __shared__ uint8_t raw[];
-  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-  constexpr int SLOTS = 512 / (4 * BN);  // TMEM holds this many stages' four groups at once
-  constexpr int TPW = BN / 4;            // tokens of an epilogue warp
-  constexpr int PAIRS = TPW / 2;
+  Smem<BN> &s = *reinterpret_cast<Smem<BN> *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = args.n >> 5, ng4 = ng & ~3;
   const int kstages = (args.n + KSTAGE - 1) / KSTAGE;
-  const int row0 = blockIdx.y * BM, tok0 = blockIdx.x * BN;
+  const int ntok = (args.count + BN - 1) / BN;
+  const int tiles = ntok * ((args.rows + BM - 1) / BM);
 
+  // the offset MMAs' constant operands, written through the generic proxy and made visible to the tensor cores
+  for (int i = threadIdx.x; i < BM * 16 / 2; i += THREADS)
+    reinterpret_cast<uint32_t *>(s.ka)[i] = F16_512 | (F16_512 << 16);
+  for (int i = threadIdx.x; i < 4 * BN * 16 / 2; i += THREADS) {
+    reinterpret_cast<uint32_t *>(s.kb_plus)[i] = F16_1536 | (F16_1536 << 16);
+    reinterpret_cast<uint32_t *>(s.kb_minus)[i] = F16_MINUS_1536 | (F16_MINUS_1536 << 16);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; i++) {
       mbar_init(&s.full[i], 1);
@@ -204,6 +254,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s.slot_full[i], 1);
       mbar_init(&s.slot_empty[i], EPI_WARPS);
     }
+    mbar_init(&s.mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // TMEM: 512 columns, the whole of this SM's (one block per SM)
@@ -215,135 +266,156 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
+  if (warp < EPI_WARP0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_SMALL));
   if (warp == 0) {
     // ---- producer: each stage's weights, activations and both scale tiles on one barrier
     if (lane == 0) {
-      const int wy = args.w_row0 + row0;
       constexpr uint32_t bytes = BM * KSTAGE + BN * KSTAGE + BM * 16 + BN * 16;
-      for (int k = 0; k < kstages; k++) {
-        const int st = k % STAGES;
-        if (!mbar_wait(&s.empty[st], ((k / STAGES) & 1) ^ 1, args.error, 1)) break;
-        mbar_expect_tx(&s.full[st], bytes);
-        tma_load_2d(s.a[st], &wmap, &s.full[st], k * KSTAGE, wy);
-        tma_load_2d(s.b[st], &xmap, &s.full[st], k * KSTAGE, tok0);
-        tma_load_2d(s.ws[st], &wsmap, &s.full[st], k * 4, wy);
-        tma_load_2d(s.xs[st], &xsmap, &s.full[st], tok0, k * 4);
+      uint32_t kk = 0;
+      Ring<STAGES> ring;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int wy = args.w_row0 + (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+        for (int k = 0; k < kstages; k++, kk++, ring.next()) {
+          const int st = ring.i;
+          if (!mbar_wait(&s.empty[st], ring.phase ^ 1, args.error, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&s.full[st], bytes);
+          tma_load_2d(s.a[st], &wmap, &s.full[st], k * KSTAGE, wy);
+          tma_load_2d(s.b[st], &xmap, &s.full[st], k * KSTAGE, tok0);
+          tma_load_2d(s.ws[st], &wsmap, &s.full[st], k * 4, wy);
+          tma_load_2d(s.xs[st], &xsmap, &s.full[st], tok0, k * 4);
+        }
       }
+      // no copy may still be landing when the block ends: wait (bounded) for the last stages issued
+      for (uint32_t i = kk > (uint32_t)STAGES ? kk - STAGES : 0; i < kk; i++)
+        mbar_wait(&s.full[i % STAGES], (i / STAGES) & 1, args.error, 6);
     }
   } else if (warp == 1) {
-    // ---- MMA issue: a stage's four groups, one MMA each (K = 32, one group) into four TMEM column blocks of the
-    // stage's slot, one commit per stage. A slot is free once every epilogue warp has read it.
-    const uint32_t idesc = idesc_i8(BN);
-    for (int k = 0; k < kstages; k++) {
-      const int st = k % STAGES, slot = k % SLOTS;
-      if (!mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 2)) break;
-      if (!mbar_wait(&s.slot_empty[slot], ((k / SLOTS) & 1) ^ 1, args.error, 3)) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const int groups = min(4, ng - 4 * k);
-        for (int j = 0; j < groups; j++)
-          mma_i8(tmem + (uint32_t)((slot * 4 + j) * BN), smem_desc(s.a[st] + 32 * j), smem_desc(s.b[st] + 32 * j),
-                 idesc);
-        mma_commit(&s.slot_full[slot]);
+    // ---- MMA issue, per stage: the offset into the stage's slot (four column blocks), one i8 MMA per group on top
+    // of it, the offset taken off, one commit. A slot is free once every epilogue warp has read it.
+    const uint32_t id_i8 = idesc_i8(BN), id_f16 = idesc_f16(4 * BN);
+    const uint64_t ka = const_desc(s.ka), kplus = const_desc(s.kb_plus), kminus = const_desc(s.kb_minus);
+    Ring<STAGES> ring;
+    Ring<SLOTS> slots;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+        const int st = ring.i, slot = slots.i;
+        if (!mbar_wait(&s.full[st], ring.phase, args.error, 2) ||
+            !mbar_wait(&s.slot_empty[slot], slots.phase ^ 1, args.error, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t d = tmem + (uint32_t)(slot * 4 * BN);
+          const int groups = min(4, ng - 4 * k);
+          mma_f16(d, ka, kplus, id_f16, 0);  // 1.5 * 2^23 in every word of the slot
+          for (int j = 0; j < groups; j++)
+            mma_i8(d + (uint32_t)(j * BN), smem_desc(s.a[st] + 32 * j), smem_desc(s.b[st] + 32 * j), id_i8, 1);
+          mma_f16(d, ka, kminus, id_f16, 1);  // less 1.5 * 2^23: float(S)
+          mma_commit(&s.slot_full[slot]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
+    // every MMA issued has completed before the block frees TMEM
+    if (lane == 0) mma_commit(&s.mma_done);
+    __syncwarp();
+    mbar_wait(&s.mma_done, 0, args.error, 7);
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
     // ---- epilogue
-    const int quarter = warp % 4, sub = (warp - 2) / 4;
-    const uint32_t magic_bits = args.magic_bits;
-    const float magic = args.magic;
-    const uint64_t magic2 = pack2(__float_as_uint(magic), __float_as_uint(magic));
-    const uint64_t one2 = pack2(__float_as_uint(args.one), __float_as_uint(args.one));
+    const int quarter = warp % 4, sub = (warp - EPI_WARP0) / 4;
     const int rl = quarter * 32 + lane;  // the row within the tile
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
-    uint64_t acc[PAIRS][4];  // chain lane j of tokens 2p (low half) and 2p + 1 (high half)
+    Ring<STAGES> ring;
+    Ring<SLOTS> slots;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+      float acc[TPW][4];  // chain lane j of token t
 #pragma unroll
-    for (int p = 0; p < PAIRS; p++)
+      for (int t = 0; t < TPW; t++)
 #pragma unroll
-      for (int j = 0; j < 4; j++) acc[p][j] = 0;
-    for (int k = 0; k < kstages; k++) {
-      const int st = k % STAGES, slot = k % SLOTS;
-      mbar_wait(&s.full[st], (k / STAGES) & 1, args.error, 4);
-      const int groups = min(4, ng - 4 * k);
-      // the stage's groups' sums of this warp's tokens, then the slot goes back to the MMAs
-      mbar_wait(&s.slot_full[slot], (k / SLOTS) & 1, args.error, 5);
-      tc_fence_after();
-      uint32_t v[4][TPW];
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-        if (j < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j) * BN), v[j]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
-      const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
-      const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
-      if (4 * k + 4 <= ng4) {
-        // a whole stage below the last four: lane j of the chain takes group 4k + j, two tokens at a time
-        const uint32_t wb[4] = {__float_as_uint(w4.x), __float_as_uint(w4.y), __float_as_uint(w4.z),
-                                __float_as_uint(w4.w)};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const uint64_t w2 = pack2(wb[j], wb[j]);
-#pragma unroll
-          for (int q = 0; q < TPW / 4; q++) {
-            const uint4 x4 = *reinterpret_cast<const uint4 *>(xrow + j * BN + 4 * q);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const int p = 2 * q + h;
-              const uint64_t x2 = h ? pack2(x4.z, x4.w) : pack2(x4.x, x4.y);
-              // float(S) exactly, times (weight scale x activation scale), rounded once (kernel_relaxed.ts:45,55)
-              const uint64_t f2 = sub2(pack2(v[j][2 * p] + magic_bits, v[j][2 * p + 1] + magic_bits), magic2);
-              acc[p][j] = fma2(one2, acc[p][j], mul2(f2, mul2(w2, x2)));
-            }
-          }
-        }
-      } else {
-        // the stage with the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
+        for (int j = 0; j < 4; j++) acc[t][j] = 0.f;
+      for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+        const int st = ring.i, slot = slots.i;
+        mbar_wait(&s.full[st], ring.phase, args.error, 4);
+        const int groups = TAIL ? min(4, ng - 4 * k) : 4;
+        mbar_wait(&s.slot_full[slot], slots.phase, args.error, 5);
+        tc_fence_after();
+        const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
         const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
+        const bool whole = !TAIL || 4 * k + 4 <= ng4;
 #pragma unroll
-        for (int p = 0; p < PAIRS; p++) {
-          float r[2];
+        for (int j0 = 0; j0 < 4; j0 += GB) {
+          uint32_t v[GB][TPW];
 #pragma unroll
-          for (int h = 0; h < 2; h++) {
-            const int t = 2 * p + h;
-            float a[4];
+          for (int jj = 0; jj < GB; jj++)
+            if (j0 + jj < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j0 + jj) * BN), v[jj]);
+          tmem_wait_ld();
+          if (whole) {
+            // lane j of the chain takes group 4k + j: float(S) x (weight scale x activation scale), rounded once
+            // each (kernel_relaxed.ts:45,55), added into the lane
 #pragma unroll
-            for (int j = 0; j < 4; j++) a[j] = h ? hi(acc[p][j]) : lo(acc[p][j]);
-            float x = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), a[2]), a[3]);
+            for (int jj = 0; jj < GB; jj++) {
+              const int j = j0 + jj;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              if (j < groups) {
-                const float f = __fsub_rn(__uint_as_float(v[j][t] + magic_bits), magic);
-                x = __fadd_rn(x, __fmul_rn(f, __fmul_rn(wv[j], xrow[j * BN + t])));
+              for (int q = 0; q < TPW / 4; q++) {
+                const float4 x4 = *reinterpret_cast<const float4 *>(xrow + j * BN + 4 * q);
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                  const int t = 4 * q + h;
+                  acc[t][j] = __fadd_rn(acc[t][j], __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xv[h])));
+                }
               }
             }
-            r[h] = x;
+          } else {
+            // the stage of the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
+            // (kept in acc[t][0]), then each group in turn
+#pragma unroll
+            for (int t = 0; t < TPW; t++) {
+              float x = j0 == 0 ? __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3])
+                                : acc[t][0];
+#pragma unroll
+              for (int jj = 0; jj < GB; jj++) {
+                const int j = j0 + jj;
+                if (j < groups)
+                  x = __fadd_rn(x, __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xrow[j * BN + t])));
+              }
+              acc[t][0] = x;
+            }
           }
-          acc[p][0] = pack2(__float_as_uint(r[0]), __float_as_uint(r[1]));
+        }
+        // the slot goes back to the MMAs, the stage's shared memory to the producer
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.slot_empty[slot]);
+          mbar_arrive(&s.empty[st]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.empty[st]);
-    }
-    if (ng4 == ng) {
+      if (!TAIL) {
 #pragma unroll
-      for (int p = 0; p < PAIRS; p++) {
-        const float r0 = __fadd_rn(__fadd_rn(__fadd_rn(lo(acc[p][0]), lo(acc[p][1])), lo(acc[p][2])), lo(acc[p][3]));
-        const float r1 = __fadd_rn(__fadd_rn(__fadd_rn(hi(acc[p][0]), hi(acc[p][1])), hi(acc[p][2])), hi(acc[p][3]));
-        acc[p][0] = pack2(__float_as_uint(r0), __float_as_uint(r1));
+        for (int t = 0; t < TPW; t++)
+          acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
       }
-    }
-    const int r = row0 + rl;
-    if (r < args.rows) {
+      const int r = row0 + rl;
+      if (r < args.rows) {
 #pragma unroll
-      for (int t = 0; t < TPW; t++) {
-        const int tok = tok0 + sub * TPW + t;
-        if (tok < args.count) {
-          const float x = (t & 1) ? hi(acc[t >> 1][0]) : lo(acc[t >> 1][0]);
-          float *o = args.out + (int64_t)tok * args.out_stride + r;
-          *o = args.accumulate ? __fadd_rn(*o, x) : x;
+        for (int t = 0; t < TPW; t++) {
+          const int tok = tok0 + sub * TPW + t;
+          if (tok < args.count) {
+            float *o = args.out + (int64_t)tok * args.out_stride + r;
+            *o = args.accumulate ? __fadd_rn(*o, acc[t][0]) : acc[t][0];
+          }
         }
       }
     }
@@ -373,6 +445,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   }
   return fn;
 }
+
+template <int BN>
+size_t smem_bytes() {
+  return sizeof(Smem<BN>) + 1024;
+}
+
+// per device (bit d): the kernels' shared-memory opt-in done, and the SM count
+std::atomic<uint64_t> opted{0};
+int sm_counts[64];
 
 }  // namespace
 
@@ -410,38 +491,84 @@ int make_token_scale_map(CUtensorMap *map, const float *base, int64_t tokens, in
                   CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-size_t gemm_smem_bytes() { return sizeof(Smem) + 1024; }
+size_t gemm_smem_bytes() { return smem_bytes<64>(); }
 
-int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &given, int bn, cudaStream_t stream) {
-  GemmArgs args = given;
-  args.magic_bits = MAGIC_BITS;
-  args.magic = MAGIC;
-  args.one = 1.0f;
-  if (args.count <= 0 || args.rows <= 0) return 0;
-  if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
-  if (bn != 16 && bn != 32) return fail(B200FWD_EINVAL, "gemm: BN must be 16 or 32");
-  const size_t smem = gemm_smem_bytes();
-  dim3 grid((args.count + bn - 1) / bn, (args.rows + BM - 1) / BM);
-  static std::atomic<uint64_t> opted{0};
+int gemm_sms() {
   int device = 0;
   B200_CUDA(cudaGetDevice(&device));
-  const uint64_t bit = device < 64 ? (1ull << device) : 0;
-  if (!bit || !(opted.load() & bit)) {
-    CHECK_RC(prepare_gemm());
-    if (bit) opted.fetch_or(bit);
+  if (device < 0 || device >= 64) return 148;
+  if (!(opted.load() & (1ull << device))) CHECK_RC(prepare_gemm());
+  return sm_counts[device];
+}
+
+int choose_gemm_bn(int rows, int count, int sms, int widest) {
+  // B200FWD_GEMM_BN=16|32|64 fixes the width (a tuning knob for measurements; within what the token maps allow)
+  static const int fixed = [] {
+    const char *v = getenv("B200FWD_GEMM_BN");
+    const int b = v ? atoi(v) : 0;
+    return b == 16 || b == 32 || b == 64 ? b : 0;
+  }();
+  if (fixed && fixed <= widest && (fixed == 16 || fixed <= count)) return fixed;
+  // a stage of a tile costs a fixed part (the pipeline's waits, TMEM and scale loads, the MMA chain) and a part that
+  // grows with its BN columns (every column is computed): measured, about 1100 + 17 BN cycles, so 64 columns' worth
+  // of fixed cost; a block walks ceil(tiles / SMs) tiles
+  const int row_tiles = (rows + BM - 1) / BM;
+  int best = 16;
+  int64_t best_cost = INT64_MAX;
+  for (int bn = 16; bn <= widest; bn *= 2) {
+    if (bn > 16 && bn > count) break;
+    const int64_t tiles = (int64_t)row_tiles * ((count + bn - 1) / bn);
+    const int64_t per_block = (tiles + sms - 1) / sms;
+    const int64_t cost = per_block * (bn + 64);
+    if (cost <= best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
   }
+  return best;
+}
+
+int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &given, int bn, cudaStream_t stream) {
+  const GemmArgs &args = given;
+  if (args.count <= 0 || args.rows <= 0) return 0;
+  if (args.n % 32) return fail(B200FWD_EINVAL, "gemm: n must be whole groups of 32");
+  if (bn != 16 && bn != 32 && bn != 64) return fail(B200FWD_EINVAL, "gemm: BN must be 16, 32 or 64");
+  const int sms = gemm_sms();
+  if (sms <= 0) return sms < 0 ? sms : fail(B200FWD_ECUDA, "gemm: no SM count");
+  const int64_t tiles = (int64_t)((args.rows + BM - 1) / BM) * ((args.count + bn - 1) / bn);
+  const dim3 grid((unsigned)std::min<int64_t>(tiles, sms));
+  const bool tail = (args.n / 32) % 4 != 0;
+#define B200_GEMM_LAUNCH(W, T) \
+  q8_gemm_tc<W, T><<<grid, THREADS, smem_bytes<W>(), stream>>>(maps.w, maps.x, maps.ws, maps.xs, args)
   if (bn == 16)
-    q8_gemm_tc<16><<<grid, THREADS, smem, stream>>>(maps.w, maps.x, maps.ws, maps.xs, args);
+    tail ? B200_GEMM_LAUNCH(16, true) : B200_GEMM_LAUNCH(16, false);
+  else if (bn == 32)
+    tail ? B200_GEMM_LAUNCH(32, true) : B200_GEMM_LAUNCH(32, false);
   else
-    q8_gemm_tc<32><<<grid, THREADS, smem, stream>>>(maps.w, maps.x, maps.ws, maps.xs, args);
+    tail ? B200_GEMM_LAUNCH(64, true) : B200_GEMM_LAUNCH(64, false);
+#undef B200_GEMM_LAUNCH
   B200_LAUNCHED("q8_gemm_tc");
   return 0;
 }
 
 int prepare_gemm() {
-  const size_t smem = gemm_smem_bytes();
-  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int device = 0;
+  B200_CUDA(cudaGetDevice(&device));
+#define B200_GEMM_OPT_IN(W, T) \
+  B200_CUDA(cudaFuncSetAttribute(q8_gemm_tc<W, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<W>()))
+  B200_GEMM_OPT_IN(16, false);
+  B200_GEMM_OPT_IN(16, true);
+  B200_GEMM_OPT_IN(32, false);
+  B200_GEMM_OPT_IN(32, true);
+  B200_GEMM_OPT_IN(64, false);
+  B200_GEMM_OPT_IN(64, true);
+#undef B200_GEMM_OPT_IN
+  if (device >= 0 && device < 64) {
+    int sms = 0;
+    B200_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    sm_counts[device] = sms;
+    opted.fetch_or(1ull << device);
+  }
   return 0;
 }
 

@@ -1,4 +1,4 @@
-// gemm_tc.h — the tensor-core int8 matmul (gemm_tc.cu) for count >= 16 tokens.
+// gemm_tc.h — the tensor-core int8 matmul (gemm_tc.cu) for prompt blocks and batched tokens.
 #pragma once
 
 #include <cuda.h>
@@ -14,12 +14,6 @@ struct GemmArgs {
   int w_row0;        // this matrix's first row in the weight view (a layer's offset)
   int64_t out_stride;
   int accumulate;    // out += result
-  // 0x4B400000 and 12582912.0f, handed over at run time: an int32 S below 2^22 in magnitude is float(S) exactly
-  // as (the float with bits S + magic_bits) - magic. (As literals the compiler turns the pair back into a
-  // conversion instruction, a far slower pipe.)
-  uint32_t magic_bits;
-  float magic;
-  float one;  // 1.0f, at run time: the chains add as fma(one, acc, product) (gemm_tc.cu, pair helpers)
 };
 
 // the four TMA maps of one matmul
@@ -40,7 +34,12 @@ int make_scale_map(CUtensorMap *map, const float *base, int64_t groups, int64_t 
 // box_tokens tokens x 4 groups
 int make_token_scale_map(CUtensorMap *map, const float *base, int64_t tokens, int64_t groups, int64_t row_floats,
                          int box_tokens);
+// bn: tokens of a tile, 16, 32 or 64 (the token map's box); a persistent grid of at most one block per SM
 int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream);
+// the tile width (16, 32 or 64, at most `widest`) that spreads rows x count best over `sms` SMs
+int choose_gemm_bn(int rows, int count, int sms, int widest);
+// the current device's SM count (after its opt-in)
+int gemm_sms();
 // the kernels' shared-memory opt-in on the current device (before any graph capture)
 int prepare_gemm();
 size_t gemm_smem_bytes();

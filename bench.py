@@ -58,9 +58,10 @@ def parse():
     p.add_argument("--cpu-prompt", type=int, default=16)
     p.add_argument("--cpu-gen", type=int, default=8)
     p.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "stories15m"])
-    p.add_argument("--config", default="c5", choices=["c5", "c4"],
+    p.add_argument("--config", default="c5", choices=["c5", "c4", "c3"],
                    help="c5: the end-to-end line (default); c4: only the int8 matmul sweep over the 8B projection "
-                        "shapes at M = 1, 8, 64, 512 (also part of the c5 line)")
+                        "shapes at M = 1, 8, 64, 512; c3: only decode attention over 64 sequences with contexts "
+                        "U[512, 8192] (both also part of the c5 line)")
     p.add_argument("--matmul", default=None, metavar="ROWSxN",
                    help="time the int8 matmul alone (b200k_matmul_q8s) at ROWSxN with --seqs tokens, one matrix of "
                         "random weights on the device: the small case the kernel profiles are captured on")
@@ -307,6 +308,71 @@ def c4_sweep(eng, peaks, counts=(1, 8, 64, 512), reps=2):
             "peak_hbm_gbs": hbm, "int8_tops_peak": int8_tops, "table": out}
 
 
+def c3_decode_attention(peaks, reps=5):
+    """Decode attention at the Llama-3-8B shape (b200k_attention_batch, exact order): 64 sequences, one query token
+    each, contexts drawn from U[512, 8192] (seed 2), 32 query / 8 key-value heads of 128, float16 cache N(0, 1)
+    (2.1 GB with the unused tails; 1.14 GB read, far above L2). Bytes: every sequence's keys and values read once
+    (sum of contexts x 8 x 128 x 2 x 2) + the queries read and the outputs written; HBM-bound."""
+    import ctypes
+
+    import torch
+
+    from b200fwd import abi
+
+    lib = abi.load()
+    nh, nkv, hs, seqs = 32, 8, 128, 64
+    kvd = nkv * hs
+    ctx = np.random.default_rng(2).integers(512, 8193, seqs).astype(np.int32)
+    P = int(ctx.max())
+    g = torch.Generator(device="cuda").manual_seed(2)
+    kc = torch.randn((seqs, P, kvd), generator=g, device="cuda", dtype=torch.float32).half()
+    vc = torch.randn((seqs, P, kvd), generator=g, device="cuda", dtype=torch.float32).half()
+    q = torch.randn((seqs, nh * hs), generator=g, device="cuda", dtype=torch.float32)
+    out = torch.empty_like(q)
+    att = torch.empty((seqs, nh, P), device="cuda", dtype=torch.float32)
+    seq = torch.arange(seqs, dtype=torch.int32, device="cuda")
+    pos = torch.from_numpy(ctx - 1).to("cuda")
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def launch():
+        abi.check(lib.b200k_attention_batch(ptr(out), ptr(q), ptr(kc), ptr(vc), ptr(att), ptr(seq), ptr(pos), seqs,
+                                            P * kvd, P, nh, nkv, hs, 1, ctypes.c_void_p(stream)), "attention_batch")
+
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        launch()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / reps
+    nbytes = float(ctx.sum()) * kvd * 2 * 2 + 2 * seqs * nh * hs * 4
+    hbm = float(peaks["hbm_gbs"])
+    gbs = nbytes / (us * 1e-6) / 1e9
+    res = {"what": "decode attention, 64 sequences x 1 token, contexts U[512, 8192] seed 2, 32/8 heads of 128, "
+                   "float16 cache, exact order (b200k_attention_batch)", "us": us, "bytes": nbytes,
+           "gb_s": gbs, "hbm_frac": gbs / hbm, "peak_hbm_gbs": hbm, "sum_context": int(ctx.sum()),
+           "tokens_per_s": seqs / (us * 1e-6)}
+    del kc, vc, att
+    torch.cuda.empty_cache()
+    return res
+
+
+def c3_arm(args):
+    """bench.py --config c3: decode attention alone (one GPU)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    peaks, which = measured_peaks()
+    res = c3_decode_attention(peaks)
+    res["peak_source"] = which
+    print(json.dumps({"config": "c3", **res}), flush=True)
+    return 0
+
+
 def c4_arm(args):
     """bench.py --config c4: the matmul sweep alone on the 8B-shape engine (one GPU)."""
     import torch
@@ -442,6 +508,7 @@ def b200_arm(args):
         roof = matmul_roofline(eng, S, peaks)
         roof["peak_source"] = which
         c4 = c4_sweep(eng, peaks)
+        c3 = c3_decode_attention(peaks)
         cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
         # the same oracle on one thread, a shorter sample (4 prompt tokens + 2 greedy steps)
         one = argparse.Namespace(**{**vars(args), "cpu_prompt": 4, "cpu_gen": 2})
@@ -472,6 +539,7 @@ def b200_arm(args):
                                      "sample": f"1 sequence: 4 prompt tokens (one block) + 2 greedy steps of the same "
                                                f"model ({cpu1_dt:.1f} s)"},
             "c4_matmul": c4,
+            "c3_decode_attention": c3,
             "gpu_launches": launches // max(1, args.steps) * args.steps,
             "clocks": clk,
         }
@@ -536,6 +604,8 @@ def main():
         return matmul_arm(args)
     if args.config == "c4":
         return c4_arm(args)
+    if args.config == "c3":
+        return c3_arm(args)
     return b200_arm(args)
 
 

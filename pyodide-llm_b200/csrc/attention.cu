@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cstdint>
+#include <cstdlib>
 
 #include "common.h"
 #include "exact.cuh"
@@ -519,8 +520,23 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     B200_LAUNCHED("attn_scores_decode");
     attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
     B200_LAUNCHED("attn_softmax_tiled");
-    // two parts of the head per token where each part's rows are whole 16-byte pieces: twice the blocks
-    const int parts = ((hs / 2) * (HALF ? 2 : 4)) % 16 == 0 && (hs / 2) % 2 == 0 ? 2 : 1;
+    // the head's values split over `parts` blocks per token (more blocks streaming at once; the positions stay in
+    // one chain per value): the most parts, up to two (measured best at 64 sequences of 512 to 8192 positions: 4 as
+    // fast, 8 slower), whose rows are whole 16-byte pieces of an even number of values and that leave a block at
+    // least one warp (B200FWD_ATT_PARTS sets the cap, a tuning knob for measurements)
+    static const int cap = [] {
+      const char *v = getenv("B200FWD_ATT_PARTS");
+      const int c = v ? atoi(v) : 0;
+      return c == 1 || c == 2 || c == 4 || c == 8 ? c : 2;
+    }();
+    int parts = 1;
+    for (int p = cap; p > 1; p /= 2) {
+      const int dims = hs / p;
+      if (hs % p == 0 && dims % 2 == 0 && (dims * (HALF ? 2 : 4)) % 16 == 0 && G * dims / 2 >= 32) {
+        parts = p;
+        break;
+      }
+    }
     const int threads = ((G * (hs / parts / 2) + 31) / 32) * 32;
     const size_t smem_values = values_smem(hs / parts, G, HALF);
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");

@@ -142,6 +142,21 @@ int b200fwd_run(b200fwd_engine *engine, int32_t n, const int32_t *slots, const i
  * logit is not finite (what llama2_numpy.greedy raises, llama2_numpy.py:1521-1527). */
 int b200fwd_generate_greedy(b200fwd_engine *engine, int32_t n, const int32_t *slots, const int32_t *first,
                             const int32_t *pos0, int32_t steps, int32_t *out);
+/* forward.js:1837-1890 `generateMany(token, pos, history, length, count, temperature, topp, penalty, randoms,
+ * stops)`, for n slots at once: from token first[i] at position pos0[i], up to `steps` steps of generate()'s loop
+ * (public/llama2_numpy.py:1612-1650) on the device: the forward pass, the repetition penalty over the slot's last
+ * B200FWD_REPETITION_WINDOW tokens (kernel.ts:705-719 penalize; none where penalty == 1), then greedy argmax
+ * (temperature 0, numpy's argmax) or kernel.ts:808-868 sample with randoms[i * steps + step] (temperature, topp),
+ * the id fed back as the next token. recent: [n][B200FWD_REPETITION_WINDOW] the last min(recent_count[i], window)
+ * tokens of slot i's history, oldest first; recent_count[i]: the history's length. A slot ends after a stop token
+ * (stops: nstops ids, host), which is its last id. out: [n][steps] the ids (host), made[i]: how many of them slot i
+ * has. The logits never leave the device; one CUDA graph per step. B200FWD_ENOTFINITE where a step's logits have
+ * no finite largest value (llama2_numpy.py:548 NOT_FINITE). */
+#define B200FWD_REPETITION_WINDOW 64
+int b200fwd_generate_many(b200fwd_engine *engine, int32_t n, const int32_t *slots, const int32_t *first,
+                          const int32_t *pos0, int32_t steps, float temperature, float topp, float penalty,
+                          const int32_t *recent, const int32_t *recent_count, const double *randoms,
+                          const int32_t *stops, int32_t nstops, int32_t *out, int32_t *made);
 /* Forget a slot's sequence (its cache is written over from position 0 by the next run). */
 int b200fwd_reset_slot(b200fwd_engine *engine, int32_t slot);
 /* The stream the engine launches on (a cudaStream_t), for callers that time it with CUDA events. */
@@ -224,6 +239,16 @@ int b200k_swiglu(float *out, const float *h1, const float *h3, int64_t n, b200fw
 int b200k_add_inplace(float *x, const float *y, int64_t n, b200fwd_stream stream);
 /* kernel.ts:671-689 add_columns: y[j] += sum over c of a[c] * rows[c][j], c in order. */
 int b200k_add_columns(float *y, const float *rows, const float *a, int32_t count, int32_t n, b200fwd_stream stream);
+/* kernel.ts:705-719 penalize: each of the count tokens (device int32) made less likely once in logits (device):
+ * value / penalty where it is above 0, else value * penalty. */
+int b200k_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, b200fwd_stream stream);
+/* kernel.ts:808-868 sample: the token drawn from softmax(logits / temperature) over n logits (device), restricted to
+ * the nucleus where 0 < topp < 1, with the random number `random` in [0, 1), into *out (device int32): -1 where the
+ * largest logit is no finite number, -2 where the nucleus sort's bounded stack ran out. scratch: a device buffer of
+ * b200k_sample_scratch(n) bytes (the reference takes two arrays of n; this one also holds the sort's stack). */
+int b200k_sample(int32_t *out, const float *logits, int32_t n, float temperature, float topp, double random,
+                 void *scratch, b200fwd_stream stream);
+int b200k_sample_scratch(int32_t n, uint64_t *bytes);
 /* kernel.ts:695-699 argmax (first index of the largest, `>`), into *out (device int32). */
 int b200k_argmax(int32_t *out, const float *x, int32_t n, b200fwd_stream stream);
 

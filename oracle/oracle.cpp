@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cfloat>
 #include <cmath>
 #include <condition_variable>
 #include <cstdint>
@@ -487,6 +488,145 @@ int oracle_argmax(const float *x, int n) {
 // kernel.ts:15-45, one value each (tests)
 float oracle_fexp(float x) { return fexp(x); }
 float oracle_vexp(float x) { return vexp(x); }
+
+// kernel.ts:705-719 penalize: each of the count recent tokens made less likely once, however often it occurs
+void oracle_penalize(float *logits, const int32_t *tokens, int count, float penalty) {
+  for (int i = 0; i < count; i++) {
+    const int32_t token = tokens[i];
+    bool seen = false;
+    for (int j = 0; j < i; j++)
+      if (tokens[j] == token) {
+        seen = true;
+        break;
+      }
+    if (seen) continue;
+    const float value = logits[token];
+    logits[token] = value > 0 ? value / penalty : value * penalty;
+  }
+}
+
+}  // extern "C"
+
+namespace {
+
+// kernel.ts:721-775 sortNucleus / intoNucleus: the nucleus's running mass (float64), its limit and its last index
+struct Nucleus {
+  double mass = 0, limit = 0;
+  int last = -1;
+};
+
+bool into_nucleus(Nucleus &nu, const float *probs, int lo, int hi) {
+  for (int k = lo; k <= hi; k++) {
+    nu.mass += (double)probs[k];
+    if (nu.mass >= nu.limit) {
+      nu.last = k;
+      return true;
+    }
+  }
+  return false;
+}
+
+// probs[lo..hi] in descending order (index along), from the left and only as far as the nucleus reaches: quicksort
+// with a median of three, insertion sort for ranges of 13 or fewer
+void sort_nucleus(Nucleus &nu, float *probs, int32_t *index, int lo, int hi) {
+  while (hi - lo > 12) {
+    const int mid = lo + ((hi - lo) >> 1);
+    float a = probs[lo], b = probs[mid];
+    const float c = probs[hi];
+    if (a < b) std::swap(a, b);
+    if (b < c) {
+      b = c;
+      if (a < b) b = a;
+    }
+    const float pivot = b;
+    int i = lo, j = hi;
+    while (i <= j) {
+      while (probs[i] > pivot) i++;
+      while (probs[j] < pivot) j--;
+      if (i <= j) {
+        std::swap(probs[i], probs[j]);
+        std::swap(index[i], index[j]);
+        i++;
+        j--;
+      }
+    }
+    sort_nucleus(nu, probs, index, lo, j);
+    if (nu.last >= 0) return;
+    if (into_nucleus(nu, probs, j + 1, i - 1)) return;  // equal to the pivot
+    lo = i;
+  }
+  for (int i = lo + 1; i <= hi; i++) {
+    const float p = probs[i];
+    const int32_t x = index[i];
+    int j = i - 1;
+    while (j >= lo && probs[j] < p) {
+      probs[j + 1] = probs[j];
+      index[j + 1] = index[j];
+      j--;
+    }
+    probs[j + 1] = p;
+    index[j + 1] = x;
+  }
+  into_nucleus(nu, probs, lo, hi);
+}
+
+}  // namespace
+
+extern "C" {
+
+// kernel.ts:808-868 sample: a token of softmax(logits / temperature), restricted to the nucleus when 0 < topp < 1,
+// drawn with `random` in [0, 1); -1 when the largest logit is no finite number. probs, index: scratch of n each.
+int oracle_sample(const float *logits, int n, float temperature, float topp, double random, float *probs,
+                  int32_t *index) {
+  float best = logits[0];
+  for (int i = 0; i < n; i++) best = wmax(best, logits[i]);  // largest(): a NaN anywhere, order-free
+  if (!std::isfinite(best)) return -1;
+  const bool nucleus = topp > 0 && topp < 1;
+  const float floor = nucleus ? best - temperature * 16.118095f : -FLT_MAX;
+  int count = 0;
+  for (int i = 0; i < n; i++) {
+    const float v = logits[i];
+    probs[count] = v - best;
+    index[count] = i;
+    count += v >= floor ? 1 : 0;
+  }
+  const float inverse = 1.0f / temperature;
+  int i = 0;
+  for (; i + 4 <= count; i += 4)
+    for (int k = 0; k < 4; k++) probs[i + k] = vexp(probs[i + k] * inverse);
+  for (; i < count; i++) probs[i] = fexp(probs[i] / temperature);
+  double total = 0;
+  float top = 0;
+  for (i = 0; i < count; i++) {
+    total += (double)probs[i];
+    top = wmax(top, probs[i]);
+  }
+  int last = count - 1;
+  double mass = total;
+  if (nucleus) {
+    const double spread = (1.0 - (double)topp) / (double)(count > 1 ? count - 1 : 1) * total;
+    const double cutoff = spread < (double)top ? spread : (double)top;
+    int likely = 0;
+    for (int k = 0; k < count; k++) {
+      const float p = probs[k];
+      probs[likely] = p;
+      index[likely] = index[k];
+      likely += (double)p >= cutoff ? 1 : 0;
+    }
+    Nucleus nu;
+    nu.limit = (double)topp * total;
+    sort_nucleus(nu, probs, index, 0, likely - 1);
+    last = nu.last >= 0 ? nu.last : likely - 1;
+    mass = nu.mass;
+  }
+  const double target = random * mass;
+  double cumulative = 0;
+  for (int k = 0; k <= last; k++) {
+    cumulative += (double)probs[k];
+    if (cumulative > target) return index[k];
+  }
+  return index[last];
+}
 
 }  // extern "C"
 

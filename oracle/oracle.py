@@ -55,6 +55,8 @@ def load():
             "oracle_add_columns": ((P, P, P, I32, I32), None),
             "oracle_add_inplace": ((P, P, I64), None),
             "oracle_argmax": ((P, I32), ctypes.c_int),
+            "oracle_penalize": ((P, P, I32, ctypes.c_float), None),
+            "oracle_sample": ((P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_double, P, P), ctypes.c_int),
             "oracle_fexp": ((ctypes.c_float,), ctypes.c_float),
             "oracle_vexp": ((ctypes.c_float,), ctypes.c_float),
             "oracle_create": ((P, ctypes.c_size_t, ctypes.POINTER(Plan), I32, I32), P),
@@ -171,6 +173,22 @@ def add_columns(y, rows, a):
 def argmax(x):
     x = np.ascontiguousarray(x, np.float32)
     return load().oracle_argmax(_p(x), x.size)
+
+
+def penalize(logits, tokens, penalty):
+    """kernel.ts:705-719 on a copy of logits"""
+    out = np.array(logits, dtype=np.float32)
+    t = np.ascontiguousarray(tokens, np.int32)
+    load().oracle_penalize(_p(out), _p(t), t.size, float(penalty))
+    return out
+
+
+def sample(logits, temperature, topp, random):
+    """kernel.ts:808-868: the token drawn with `random` in [0, 1), -1 for logits whose largest is not finite"""
+    x = np.ascontiguousarray(logits, np.float32)
+    probs, index = np.zeros(x.size, np.float32), np.zeros(x.size, np.int32)
+    return int(load().oracle_sample(_p(x), x.size, float(temperature), float(topp), float(random), _p(probs),
+                                    _p(index)))
 
 
 def fexp(x):

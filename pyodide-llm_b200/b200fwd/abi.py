@@ -158,6 +158,11 @@ def load():
         "b200k_add_inplace": (P, P, I64, P),
         "b200k_add_columns": (P, P, P, I32, I32, P),
         "b200k_argmax": (P, P, I32, P),
+        "b200k_penalize": (P, P, I32, ctypes.c_float, P),
+        "b200k_sample": (P, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_double, P, P),
+        "b200k_sample_scratch": (I32, ctypes.POINTER(U64)),
+        "b200fwd_generate_many": (P, I32, P, P, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, P, P,
+                                  I32, P, P),
         "b200k_attention_batch": (P, P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, I32, P),
     }
     for name, args in sig.items():

@@ -82,10 +82,47 @@ class Engine:
         """forward.js:1773-1778: how many prompt tokens Python hands forwardMany at once"""
         return self._prompt_block
 
+    TOKEN_BLOCK = 16
+    REPETITION_WINDOW = 64  # public/llama2_numpy.py:545
+
     @property
     def tokenBlock(self):
-        """forward.js:1837-1840: steps per generateMany; 0, the steps go through forward() and Python's sampling"""
-        return 0
+        """forward.js:1837-1840: how many steps generate() hands generateMany at once (public/llama2_numpy.py:1612-1620)"""
+        return self.TOKEN_BLOCK
+
+    def generateMany(self, token, pos, history, length, count, temperature, topp, penalty, randoms, stops):
+        """forward.js:1830-1890 generateMany: count steps of generate() from token at pos on the device (slot 0): the
+        forward pass, the repetition penalty over the last 64 tokens of the history (the last of `history`, whose
+        whole length is `length`), then greedy argmax (temperature 0) or kernel.ts's sample with one of `randoms` a
+        step. Returns the ids (a stop token last where one came); their keys and values are in the cache as forward()
+        would have written them."""
+        ids, made = self.generate_many([0], [token], [pos], count, temperature, topp, penalty, [list(history)],
+                                       [length], [list(randoms)] if temperature != 0 else None, list(stops))
+        return [int(t) for t in ids[0][:made[0]]]
+
+    def generate_many(self, slots, first, pos0, steps, temperature, topp, penalty, histories, lengths, randoms,
+                      stops):
+        """generateMany for several slots at once: returns (ids [n][steps], made [n])."""
+        n, W = len(slots), self.REPETITION_WINDOW
+        recent = np.zeros((n, W), np.int32)
+        for i, h in enumerate(histories):
+            last = list(h)[-min(int(lengths[i]), W):] if lengths[i] else []
+            recent[i, :len(last)] = last
+        r = None
+        if temperature != 0:
+            r = np.zeros((n, steps), np.float64)
+            for i, row in enumerate(randoms):
+                row = list(row)[:steps]
+                r[i, :len(row)] = row
+        st = np.ascontiguousarray(stops, np.int32)
+        # (the arrays are held in locals until the call returns: the library reads them through bare pointers)
+        sl, fi = np.ascontiguousarray(slots, np.int32), np.ascontiguousarray(first, np.int32)
+        po, le = np.ascontiguousarray(pos0, np.int32), np.ascontiguousarray(lengths, np.int32)
+        out, made = np.zeros((n, steps), np.int32), np.zeros(n, np.int32)
+        abi.check(self._lib.b200fwd_generate_many(
+            self._h, n, _p(sl), _p(fi), _p(po), int(steps), float(temperature), float(topp), float(penalty),
+            _p(recent), _p(le), _p(r), _p(st) if st.size else None, st.size, _p(out), _p(made)), "generateMany")
+        return out, made
 
     def release(self):
         """forward.js:1915-1934"""

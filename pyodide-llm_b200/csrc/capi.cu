@@ -196,6 +196,32 @@ int b200k_add_columns(float *y, const float *rows, const float *a, int32_t count
   return guarded([&] { return launch_add_columns(y, n, rows, a, count, count, n, 1, as_stream(stream)); });
 }
 
+int b200k_penalize(float *logits, const int32_t *tokens, int32_t count, float penalty, b200fwd_stream stream) {
+  return guarded([&] {
+    if (count < 0 || (count && (!logits || !tokens))) return fail(B200FWD_EINVAL, "penalize: bad arguments");
+    if (count == 0) return 0;
+    return launch_penalize(logits, 0, tokens, count, nullptr, penalty, nullptr, 1, as_stream(stream));
+  });
+}
+
+int b200k_sample_scratch(int32_t n, uint64_t *bytes) {
+  if (n < 1 || !bytes) return fail(B200FWD_EINVAL, "sample_scratch: bad arguments");
+  *bytes = sample_scratch_words(n) * 4 + sample_stack_words() * 4;
+  return 0;
+}
+
+int b200k_sample(int32_t *out, const float *logits, int32_t n, float temperature, float topp, double random,
+                 void *scratch, b200fwd_stream stream) {
+  return guarded([&] {
+    if (!out || !logits || !scratch || n < 1) return fail(B200FWD_EINVAL, "sample: bad arguments");
+    if (reinterpret_cast<uintptr_t>(scratch) % 8) return fail(B200FWD_EINVAL, "sample: scratch must be 8-byte aligned");
+    float *probs = reinterpret_cast<float *>(scratch);
+    int32_t *stack = reinterpret_cast<int32_t *>(probs + sample_scratch_words(n));
+    return launch_sample(out, logits, 0, n, temperature, topp, nullptr, random, 0, nullptr, probs, stack, nullptr, 1,
+                         as_stream(stream));
+  });
+}
+
 int b200k_argmax(int32_t *out, const float *x, int32_t n, b200fwd_stream stream) {
   return guarded([&] {
     if (n < 1) return fail(B200FWD_EINVAL, "argmax: no values");

@@ -107,6 +107,13 @@ struct b200fwd_engine {
   int32_t *meta_h = nullptr;    // pinned host copy
   int32_t *history = nullptr;   // greedy ids [slots][steps]
   int history_len = 0;
+  // generate_many's device state: one block of int32 words and one of doubles / floats, grown as needed
+  int32_t *gm_words = nullptr;
+  size_t gm_words_len = 0;
+  double *gm_randoms = nullptr;
+  size_t gm_randoms_len = 0;
+  float *gm_scratch = nullptr;
+  size_t gm_scratch_len = 0;
   float *bound = nullptr;       // Python's logits array (host)
   std::vector<float> last_logits;
   uint64_t bytes = 0;
@@ -336,7 +343,7 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
 // the layers over n tokens whose ids, slots and positions are in meta (device); the logits of the `want` tokens
 // (their indices in want_d) into logits rows 0..want-1, and their argmax. ntiles > 0: the attention's token tiles
 // are in tiles_d; 0: every token its own. Enqueues only (graph-capturable).
-int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles) {
+int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles, bool argmax = true) {
   cudaStream_t st = e->stream;
   const int D = e->dim, QD = e->qDim, KVD = e->kvDim, HID = e->hidden, XQ = e->XQ, TP = e->TP, QKV = e->QKV;
   const int shift = e->bias;  // activations stored less the bias
@@ -367,7 +374,7 @@ int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles
                              e->picked, nullptr, 0, st, shift));
   CHECK(matmul(e, e->wcls, 0, e->logits, e->vocab, 0, want));
   CHECK(launch_add_columns(e->logits, e->vocab, e->columns, e->picked, e->nch, e->nch, e->vocab, want, st));
-  CHECK(launch_argmax(e->argmax, e->logits, e->vocab, e->vocab, want, 1, st));
+  if (argmax) CHECK(launch_argmax(e->argmax, e->logits, e->vocab, e->vocab, want, 1, st));
   return 0;
 }
 
@@ -569,6 +576,19 @@ int guarded(F &&f) {
 int set_device(b200fwd_engine *e) {
   if (!e) return fail(B200FWD_EINVAL, "no engine");
   B200_CUDA(cudaSetDevice(e->device));
+  return 0;
+}
+
+// a device buffer of at least `want` elements, reallocated (larger) when it is not
+template <typename T>
+int ensure(b200fwd_engine *e, T **p, size_t *len, size_t want) {
+  if (*len >= want) return 0;
+  B200_CUDA(cudaStreamSynchronize(e->stream));
+  release(e, *p, *len * sizeof(T));
+  *p = nullptr;
+  *len = 0;
+  CHECK(alloc(e, (void **)p, want * sizeof(T)));
+  *len = want;
   return 0;
 }
 
@@ -820,6 +840,124 @@ int b200fwd_time_matmul_kinds(b200fwd_engine *e, int32_t count, int32_t reps, fl
           (double)m.rows * m.n * (1.0 + 4.0 / 32) + (double)count * m.n * (1.0 + 4.0 / 32) + 4.0 * count * m.rows;
     }
     return check_tc(e);
+  });
+}
+
+int b200fwd_generate_many(b200fwd_engine *e, int32_t n, const int32_t *slots, const int32_t *first,
+                          const int32_t *pos0, int32_t steps, float temperature, float topp, float penalty,
+                          const int32_t *recent, const int32_t *recent_count, const double *randoms,
+                          const int32_t *stops, int32_t nstops, int32_t *out, int32_t *made) {
+  return guarded([&] {
+    CHECK(set_device(e));
+    constexpr int W = B200FWD_REPETITION_WINDOW;
+    if (n < 1 || n > std::min(e->T, 1024) || steps < 1 || !slots || !first || !pos0 || !out || !made ||
+        nstops < 0 || (nstops && !stops) || (n && !recent_count) || !(temperature >= 0) || !(penalty > 0))
+      return fail(B200FWD_EINVAL, "generate_many: bad arguments");
+    if (temperature > 0 && !randoms) return fail(B200FWD_EINVAL, "generate_many: no random numbers");
+    int maxpos = 0;
+    for (int i = 0; i < n; i++) {
+      if (slots[i] < 0 || slots[i] >= e->slots) return fail(B200FWD_EINVAL, "generate_many: slot out of range");
+      for (int j = 0; j < i; j++)
+        if (slots[j] == slots[i]) return fail(B200FWD_EINVAL, "generate_many: a slot given twice");
+      if (first[i] < 0 || first[i] >= e->vocab) return fail(B200FWD_EINVAL, "generate_many: token out of range");
+      if (pos0[i] < 0 || pos0[i] + steps > e->seqLen)
+        return fail(B200FWD_EINVAL, "generate_many: the steps run past the context");
+      if (recent_count[i] < 0) return fail(B200FWD_EINVAL, "generate_many: a negative history length");
+      for (int k = 0; k < std::min(recent_count[i], W); k++)
+        if (!recent || recent[(int64_t)i * W + k] < 0 || recent[(int64_t)i * W + k] >= e->vocab)
+          return fail(B200FWD_EINVAL, "generate_many: a history token out of range");
+      maxpos = std::max(maxpos, pos0[i] + steps - 1);
+    }
+    for (int k = 0; k < nstops; k++)
+      if (stops[k] < 0 || stops[k] >= e->vocab) return fail(B200FWD_EINVAL, "generate_many: a stop token out of range");
+    if (maxpos >= e->capacity) CHECK(grow(e, maxpos));
+    CHECK(ensure_logit_rows(e, n));
+    // the int32 state: ids [n][steps], ring [n][W], ring counts [n], done [n], made [n], stops, sampled ids [n]
+    const size_t words = (size_t)n * steps + (size_t)n * W + 4 * (size_t)n + nstops + 1 +
+                         (size_t)n * sample_stack_words();
+    CHECK(ensure(e, &e->gm_words, &e->gm_words_len, words));
+    const bool greedy = temperature == 0;
+    if (!greedy) {
+      CHECK(ensure(e, &e->gm_randoms, &e->gm_randoms_len, (size_t)n * steps));
+      CHECK(ensure(e, &e->gm_scratch, &e->gm_scratch_len, (size_t)n * sample_scratch_words(e->vocab)));
+    }
+    int32_t *ids_all = e->gm_words, *ring = ids_all + (size_t)n * steps, *ring_count = ring + (size_t)n * W;
+    int32_t *done = ring_count + n, *made_d = done + n, *stops_d = made_d + n, *chosen = stops_d + nstops + 1;
+    int32_t *stacks = chosen + n;
+    // the rings as the reference keeps them (position p of the history at p % W), from the last W tokens given
+    std::vector<int32_t> hring((size_t)n * W, 0), hcount(n), zeros(2 * (size_t)n, 0);
+    for (int i = 0; i < n; i++) {
+      const int len = recent_count[i], m = std::min(len, W);
+      for (int k = 0; k < m; k++) hring[(size_t)i * W + (len - m + k) % W] = recent[(size_t)i * W + k];
+      hcount[i] = len;
+    }
+    B200_CUDA(cudaMemcpyAsync(ring, hring.data(), hring.size() * 4, cudaMemcpyHostToDevice, e->stream));
+    B200_CUDA(cudaMemcpyAsync(ring_count, hcount.data(), (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+    B200_CUDA(cudaMemcpyAsync(done, zeros.data(), 2 * (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+    if (nstops) B200_CUDA(cudaMemcpyAsync(stops_d, stops, (size_t)nstops * 4, cudaMemcpyHostToDevice, e->stream));
+    if (!greedy)
+      B200_CUDA(cudaMemcpyAsync(e->gm_randoms, randoms, (size_t)n * steps * 8, cudaMemcpyHostToDevice, e->stream));
+    const int T = e->T;
+    int32_t *m = e->meta_h;
+    B200_CUDA(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n; i++) {
+      m[i] = first[i];
+      m[T + i] = slots[i];
+      m[2 * T + i] = pos0[i];
+      m[3 * T + i] = i;
+    }
+    m[4 * T] = 0;
+    m[4 * T + 1] = 0;
+    m[4 * T + 2] = 0;
+    B200_CUDA(cudaMemcpyAsync(e->meta, m, (size_t)(4 * T + 3) * 4, cudaMemcpyHostToDevice, e->stream));
+    // one step, captured once and replayed: every slot's forward pass, the penalty over its recent tokens, the draw
+    // (or the argmax), then the bookkeeping (a stop token or a failure ends a slot: its token and position stay, so
+    // the passes after it write its last position's keys and values again, the same numbers)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const uint64_t before = launches.load();
+    B200_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = forward_device(e, n, n, e->capacity, 0, false);
+    if (!rc && penalty != 1.0f)
+      rc = launch_penalize(e->logits, e->vocab, ring, W, ring_count, penalty, done, n, e->stream);
+    if (!rc)
+      rc = greedy ? launch_argmax(chosen, e->logits, e->vocab, e->vocab, n, 1, e->stream)
+                  : launch_sample(chosen, e->logits, e->vocab, e->vocab, temperature, topp, e->gm_randoms, 0.0, steps,
+                                  e->step_d(), e->gm_scratch, stacks, done, n, e->stream);
+    if (!rc)
+      rc = launch_advance_sampled(e->tokens_d(), e->pos_d(), chosen, ids_all, steps, e->step_d(), n, e->logits,
+                                  e->vocab, greedy ? 1 : 0, ring, W, ring_count, stops_d, nstops, done, made_d,
+                                  e->bad_d(), e->stream);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+    const uint64_t per_step = launches.load() - before;
+    launches.fetch_sub(per_step);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    for (int s = 0; s < steps; s++) {
+      ce = cudaGraphLaunch(exec, e->stream);
+      if (ce != cudaSuccess) break;
+      launches.fetch_add(per_step);
+    }
+    cudaError_t se = cudaStreamSynchronize(e->stream);
+    cudaGraphExecDestroy(exec);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphLaunch");
+    if (se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
+    B200_CUDA(cudaMemcpy(out, ids_all, (size_t)n * steps * 4, cudaMemcpyDeviceToHost));
+    B200_CUDA(cudaMemcpy(made, made_d, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    CHECK(check_tc(e));
+    int32_t bad = 0;
+    B200_CUDA(cudaMemcpy(&bad, e->bad_d(), 4, cudaMemcpyDeviceToHost));
+    if (bad == 1)
+      return fail(B200FWD_ENOTFINITE,
+                  "The model computed logits that are not finite numbers (NaN or infinity), so no token can be drawn.");
+    if (bad == 2) return fail(B200FWD_EUNSUPPORTED, "generate_many: the nucleus sort ran past its stack");
+    return 0;
   });
 }
 

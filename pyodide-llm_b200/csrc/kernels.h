@@ -94,6 +94,24 @@ int launch_int8_sums(int32_t *out, const int8_t *w, int64_t groups, cudaStream_t
 // *bad = 1 where the chosen logit (logits[i * vocab + id]) is not finite
 int launch_advance(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps, int32_t *step,
                    int count, const float *logits, int64_t vocab, int32_t *bad, cudaStream_t stream);
+// kernel.ts:705-719 penalize for count sequences (logits rows stride apart): recent [count][window] tokens, the first
+// min(recent_count[s], window) of row s used (recent_count null: all window); rows with done[s] (nullable) left alone
+int launch_penalize(float *logits, int64_t stride, const int32_t *recent, int window, const int32_t *recent_count,
+                    float penalty, const int32_t *done, int count, cudaStream_t stream);
+// kernel.ts:808-868 sample for count sequences: out[s] the id drawn from logits row s with random[s * rstride + *step]
+// (step nullable: 0; random null: random0), -1 where the largest logit is not finite, -2 where the nucleus sort's
+// stack ran out; scratch sample_scratch_words(n) floats and stacks sample_stack_words() int32 per sequence; done[s]
+// (nullable) skips s
+int launch_sample(int32_t *out, const float *logits, int64_t stride, int n, float temperature, float topp,
+                  const double *random, double random0, int64_t rstride, const int32_t *step, float *scratch,
+                  int32_t *stacks, const int32_t *done, int count, cudaStream_t stream);
+size_t sample_scratch_words(int n);
+size_t sample_stack_words();
+// the bookkeeping of one sampled step (sampling.cu advance_sampled_kernel)
+int launch_advance_sampled(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps,
+                           int32_t *step, int count, const float *logits, int64_t vocab, int greedy, int32_t *recent,
+                           int window, int32_t *recent_count, const int32_t *stops, int nstops, int32_t *done,
+                           int32_t *made, int32_t *bad, cudaStream_t stream);
 // kernel.ts:330-342 rmsnorm of count rows (stride floats apart)
 int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps, int count, int64_t stride,
                    cudaStream_t stream);

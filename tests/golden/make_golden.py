@@ -10,7 +10,11 @@ recorded so that the tests can make it again without the reference):
   - numpy_<name>.npz: the reference NumPy engine's logits (`Llama.forward`, public/llama2_numpy.py:1310-1465) on
     its own greedy text from BOS, at POSITIONS positions: forward.js is held to these by the line of
     tests/forward-check.mjs:2-9,437 (the most likely token the same at >= 85% of positions, perplexity within 5%).
-Besides: quantize.npz (the reference's quantize() of a seeded matrix), rope.npz (its rope_tables()).
+Besides: quantize.npz (the reference's quantize() of a seeded matrix), rope.npz (its rope_tables()), and
+generate_tiny_gqa.npz: the unmodified `Llama(None, tokenizer, dtype="int8", external=...).generate(prompt,
+temperature=0)` (public/llama2_numpy.py:1565-1671) driving a stand-in engine that serves forward.js's members from the
+oracle (OracleExternal below): the prompt's token ids, every block and token it fed the engine (forwardMany blocks of
+promptBlock, then forward), and the ids its greedy sampling chose.
 """
 import hashlib
 import json
@@ -71,6 +75,115 @@ class Capture:
         return Stub()
 
 
+class OracleExternal:
+    """TEST INFRASTRUCTURE: forward.js's external() (public/forward.js:571-590) whose engine answers from the oracle
+    (oracle/oracle.py: the C++ restatement of forward.js run()), recording every call the caller makes."""
+
+    def __init__(self, data, prompt_block=16):
+        self.data, self.size, self.prompt_block, self.fed = data, len(data), prompt_block, []
+
+    def read(self, offset, length):
+        return self.data[offset:offset + length]
+
+    def start(self, plan):
+        sys.path.insert(0, str(REPO / "oracle"))
+        import oracle
+
+        outer = self
+
+        class Engine:
+            backend = "oracle (test stand-in)"
+            promptBlock = outer.prompt_block
+
+            def __init__(self):
+                self.ref = oracle.OracleEngine(outer.data, plan, half_keys=-1, threads=2)
+                self.logits = None
+
+            def bind(self, array):
+                self.logits = array
+
+            def forward(self, token, pos, needLogits=True):
+                outer.fed.append((int(pos), [int(token)], bool(needLogits)))
+                out = self.ref.forward(int(token), int(pos), needLogits)
+                if needLogits:
+                    self.logits[:] = out
+
+            def forwardMany(self, tokens, pos):
+                outer.fed.append((int(pos), [int(t) for t in tokens], False))
+                self.ref.forward_many(list(tokens), int(pos))
+
+        return Engine()
+
+
+PROMPT = "Once upon a time, there was a little girl named Lily."
+GENERATE_STEPS = 120
+
+
+def generate_fixture(llama2_numpy, name="tiny_gqa"):
+    header, seed, norm, _ = MODELS[name]
+    data = ck.synthetic_checkpoint(header, seed=seed, norm=norm)
+    ext = OracleExternal(data)
+    model = llama2_numpy.Llama(None, tokenizer_bin(abs(header[5])), dtype="int8", external=ext)
+    chosen = []
+    sample = model.sample
+
+    def recording(logits, temperature, topp, rng):
+        token = sample(logits, temperature, topp, rng)
+        chosen.append(int(token))
+        return token
+
+    model.sample = recording
+    text = "".join(model.generate(PROMPT, steps=GENERATE_STEPS, temperature=0.0))
+    prompt = model.tokenizer.encode(PROMPT, model.specials)
+    fed_pos = np.array([p + i for p, toks, _ in ext.fed for i in range(len(toks))], np.int32)
+    fed_tok = np.array([t for _, toks, _ in ext.fed for t in toks], np.int32)
+    fed_call = np.array([i for i, (_, toks, _) in enumerate(ext.fed) for _ in toks], np.int32)
+    np.savez_compressed(HERE / f"generate_{name}.npz", prompt=np.array(prompt, np.int32), ids=np.array(chosen, np.int32),
+                        steps=np.array(GENERATE_STEPS), prompt_block=np.array(ext.prompt_block), fed_pos=fed_pos,
+                        fed_tok=fed_tok, fed_call=fed_call, sha256=np.frombuffer(hashlib.sha256(data).digest(), np.uint8))
+    print(name, "generate:", len(prompt), "prompt tokens,", len(chosen), "chosen,", len(ext.fed), "engine calls,",
+          len(text), "characters")
+
+
+class Drawn:
+    """A generator whose random() gives the numbers it was made with, in order (so that a test can give the same)."""
+
+    def __init__(self, numbers):
+        self.numbers = list(numbers)
+
+    def random(self):
+        return self.numbers.pop(0)
+
+
+def sample_fixture(llama2_numpy):
+    """sample.npz: the reference's NumPy sampler (Llama.sample and Llama.penalize, public/llama2_numpy.py:1529-1563,
+    1514-1518) on seeded logits at several temperatures and top-p values, with the random numbers it drew."""
+    rng = np.random.default_rng(17)
+    logits, temps, topps, randoms, chosen, penalized, histories = [], [], [], [], [], [], []
+    for case in range(48):
+        vocab = 1000
+        x = (rng.standard_normal(vocab) * rng.choice([0.3, 1.0, 3.0, 8.0])).astype(np.float32)
+        t = float(rng.choice([0.3, 0.7, 1.0, 1.6]))
+        p = float(rng.choice([0.5, 0.9, 0.95, 1.0]))
+        history = [int(v) for v in rng.integers(0, vocab, 80)]
+        pen = x.copy()
+        llama2_numpy.Llama.penalize(None, pen, history, 1.3)
+        for _ in range(8):
+            r = float(rng.random())
+            token = llama2_numpy.Llama.sample(None, pen.copy(), t, p, Drawn([r]))
+            logits.append(x)
+            temps.append(t)
+            topps.append(p)
+            randoms.append(r)
+            chosen.append(token)
+            penalized.append(pen)
+            histories.append(history)
+    np.savez_compressed(HERE / "sample.npz", logits=np.stack(logits), temperature=np.array(temps, np.float32),
+                        topp=np.array(topps, np.float32), random=np.array(randoms), chosen=np.array(chosen, np.int32),
+                        penalized=np.stack(penalized), history=np.array(histories, np.int32))
+    print("sample:", len(chosen), "draws")
+
+
 def main(reference):
     sys.path.insert(0, str(Path(reference) / "public"))
     import llama2_convert
@@ -108,6 +221,8 @@ def main(reference):
     cos8, sin8 = llama2_numpy.rope_tables(64, 128, 500000.0)
     np.savez_compressed(HERE / "rope.npz", cos=cos.astype(np.float32), sin=sin.astype(np.float32),
                         cos8b=cos8.astype(np.float32), sin8b=sin8.astype(np.float32))
+    generate_fixture(llama2_numpy)
+    sample_fixture(llama2_numpy)
 
 
 if __name__ == "__main__":

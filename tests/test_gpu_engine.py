@@ -220,3 +220,112 @@ def test_time_matmuls_leaves_the_sequence_alone(stories):
         runs.append(last)
         eng.release()
     assert np.array_equal(bits(runs[0]), bits(runs[1]))
+
+
+def test_generate_drives_the_engine_like_the_reference():
+    """The reference's generate() (public/llama2_numpy.py:1565-1671), unmodified, drove an oracle-backed engine to
+    make generate_tiny_gqa.npz (tests/golden/make_golden.py): 54 prompt tokens in forwardMany blocks, then 66 greedy
+    steps through forward(). The same loop over b200fwd.forward.external(...).start(plan) (this engine's promptBlock:
+    one block) chooses the same 66 ids."""
+    from test_oracle_golden import generate_like_the_reference
+
+    data, plan, _ = golden_model("tiny_gqa")
+    g = np.load(GOLDEN / "generate_tiny_gqa.npz")
+    eng = external(data).start(plan)
+    logits = np.zeros(plan["vocab_size"], np.float32)
+    eng.bind(logits)
+    eng.bound_logits = logits
+    calls, chosen = generate_like_the_reference(eng, [int(t) for t in g["prompt"]], int(g["steps"]))
+    assert chosen == [int(t) for t in g["ids"]]
+    assert calls[0] == (0, [1] + [int(t) for t in g["prompt"][:-1]])  # the whole prompt in one block here
+    eng.release()
+
+
+def oracle_generate(data, plan, prompt, steps, temperature, topp, penalty, randoms, stops):
+    """generate()'s sampling loop (public/llama2_numpy.py:1612-1650, with the kernel sampler of :1468-1512) on the
+    oracle: forward, penalize over the last 64 tokens of the history, sample (or argmax), stop tokens."""
+    ref = oracle.OracleEngine(data, plan, threads=2)
+    ref.forward_many([1] + prompt[:-1], 0)
+    history, token, pos, ids = [1] + prompt, prompt[-1], len(prompt), []
+    while pos < steps:
+        logits = ref.forward(token, pos)
+        if penalty != 1.0:
+            logits = oracle.penalize(logits, history[-64:], penalty)
+        nxt = int(np.argmax(logits)) if temperature == 0 else oracle.sample(logits, temperature, topp,
+                                                                            randoms[len(ids)])
+        ids.append(nxt)
+        if nxt in stops:
+            break
+        history.append(nxt)
+        token, pos = nxt, pos + 1
+    ref.close()
+    return ids
+
+
+def engine_generate(eng, prompt, steps, temperature, topp, penalty, randoms, stops):
+    """generate()'s loop over an engine with generateMany (public/llama2_numpy.py:1612-1650): blocks of tokenBlock
+    steps, a random number per step, the history's last 64 tokens and its length, stop tokens."""
+    eng.forwardMany([1] + prompt[:-1], 0)
+    history, token, pos, ids = [1] + prompt, prompt[-1], len(prompt), []
+    while pos < steps:
+        many = min(eng.tokenBlock, steps - pos)
+        rs = list(randoms[len(ids):len(ids) + many]) if temperature != 0 else []
+        chosen = eng.generateMany(token, pos, history[-64:], len(history), many, temperature, topp, penalty, rs,
+                                  sorted(stops))
+        ended = False
+        for nxt in chosen:
+            ids.append(nxt)
+            if nxt in stops:
+                ended = True
+                break
+            history.append(nxt)
+            token, pos = nxt, pos + 1
+        if ended:
+            break
+    return ids
+
+
+@pytest.mark.parametrize("temperature,topp,penalty", [(0.0, 0.9, 1.3), (0.8, 0.9, 1.2), (1.0, 1.0, 1.0),
+                                                      (0.6, 0.5, 1.0)])
+def test_generate_many_is_generates_loop(temperature, topp, penalty):
+    """generateMany on the device (b200fwd_generate_many: forward, penalize, sample or argmax, in one CUDA graph a
+    step) gives the ids of generate()'s loop on the oracle with the same random numbers, to the id, over 70 steps in
+    blocks of tokenBlock; then again with the 9th id made a stop token: the run ends there, that id last."""
+    data, plan, _ = golden_model("tiny_gqa")
+    rng = np.random.default_rng(4)
+    prompt = [int(t) for t in rng.integers(3, 320, 20)]
+    randoms = [float(v) for v in rng.random(80)]
+    steps = len(prompt) + 70
+    want = oracle_generate(data, plan, prompt, steps, temperature, topp, penalty, randoms, set())
+    eng = Engine(data, plan)
+    assert eng.tokenBlock > 0
+    got = engine_generate(eng, prompt, steps, temperature, topp, penalty, randoms, set())
+    eng.release()
+    assert got == want
+    stop = {want[8]}
+    want2 = oracle_generate(data, plan, prompt, steps, temperature, topp, penalty, randoms, stop)
+    eng = Engine(data, plan)
+    got2 = engine_generate(eng, prompt, steps, temperature, topp, penalty, randoms, stop)
+    eng.release()
+    assert got2 == want2 and got2[-1] in stop and len(got2) <= 9
+
+
+def test_generate_many_slots_are_independent():
+    """Three slots sampled in one b200fwd_generate_many call give each slot's ids alone."""
+    data, plan, _ = golden_model("tiny_gqa")
+    rng = np.random.default_rng(6)
+    prompts = [[1] + [int(t) for t in rng.integers(3, 320, n)] for n in (9, 17, 4)]
+    randoms = rng.random((3, 12))
+    alone = []
+    for i, p in enumerate(prompts):
+        e = Engine(data, plan)
+        e.forwardMany(p[:-1], 0)
+        alone.append(e.generateMany(p[-1], len(p) - 1, p[-64:], len(p), 12, 0.9, 0.9, 1.1, list(randoms[i]), []))
+        e.release()
+    eng = Engine(data, plan, slots=3)
+    for i, p in enumerate(prompts):
+        eng.run([i] * (len(p) - 1), p[:-1], list(range(len(p) - 1)))
+    ids, made = eng.generate_many([0, 1, 2], [p[-1] for p in prompts], [len(p) - 1 for p in prompts], 12, 0.9, 0.9,
+                                  1.1, [p for p in prompts], [len(p) for p in prompts], randoms, [])
+    for i in range(3):
+        assert list(ids[i][:made[i]]) == alone[i], i

@@ -318,3 +318,39 @@ def test_bad_arguments_are_refused(lib):
     assert rc == abi.EINVAL and "null" in abi.last_error()
     rc = lib.b200k_quantize_x(None, None, None, 32, 7, 1, 32, 32, 1, None)
     assert rc == abi.EINVAL and "bias" in abi.last_error()
+
+
+def test_penalize_and_sample_are_the_oracles(lib):
+    """kernel.ts:705-868 penalize and sample (b200k_penalize, b200k_sample) against the oracle's restatement, to the
+    bit and the id, on the NumPy-sampler fixture's logits (tests/golden/sample.npz: temperatures 0.3-1.6, top-p 0.5,
+    0.9, 0.95 and 1, with their random numbers), on a 128256-wide vocabulary, and on the edges (NaN, +inf)."""
+    from conftest import GOLDEN
+
+    g = np.load(GOLDEN / "sample.npz")
+    size = ctypes.c_uint64()
+
+    def draw(x, t, p, r):
+        abi.check(lib.b200k_sample_scratch(x.size, ctypes.byref(size)))
+        scratch = empty(int(size.value) // 4 + 2, np.int32)
+        out, dx = full(1, -9, np.int32), dev(np.ascontiguousarray(x, np.float32))
+        abi.check(lib.b200k_sample(ptr(out), ptr(dx), x.size, float(t), float(p), float(r), ptr(scratch), None))
+        return int(host(out)[0])
+
+    for i in range(0, g["chosen"].size, 3):
+        hist = np.ascontiguousarray(g["history"][i][-64:], np.int32)
+        dx, dh = dev(g["logits"][i]), dev(hist)
+        abi.check(lib.b200k_penalize(ptr(dx), ptr(dh), hist.size, np.float32(1.3), None))
+        pen = host(dx)
+        assert np.array_equal(bits(pen), bits(oracle.penalize(g["logits"][i], hist, 1.3))), i
+        want = oracle.sample(pen, g["temperature"][i], g["topp"][i], g["random"][i])
+        assert draw(pen, g["temperature"][i], g["topp"][i], g["random"][i]) == want, i
+    rng = np.random.default_rng(8)
+    for scale, t, p in ((6.0, 0.8, 0.9), (0.5, 1.0, 0.95), (3.0, 0.7, 1.0)):
+        x = (rng.standard_normal(128256) * scale).astype(np.float32)
+        for r in (0.0, 0.37, 0.999):
+            assert draw(x, t, p, r) == oracle.sample(x, t, p, r), (scale, t, p, r)
+    x = np.zeros(100, np.float32)
+    x[3] = np.nan
+    assert draw(x, 1.0, 0.9, 0.5) == -1
+    x[3] = np.inf
+    assert draw(x, 1.0, 0.9, 0.5) == -1

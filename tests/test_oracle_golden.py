@@ -236,3 +236,90 @@ def test_oracle_engine_against_numpy(name):
     k1, v1 = e.keys_values(0, len(tokens))
     k3, v3 = e3.keys_values(0, len(tokens))
     assert np.array_equal(k1, k3) and np.array_equal(v1, v3)
+
+
+def generate_like_the_reference(engine, prompt, steps, bos=1, stops=(1,)):
+    """public/llama2_numpy.py:1565-1671 generate(prompt, temperature=0) as it drives an engine with forwardMany
+    (`Llama.external_forward`, :1276-1283): [BOS] + prompt[:-1] through forwardMany in blocks of promptBlock, then
+    forward(token, pos) and greedy sampling (np.argmax, :1521-1527) from the last prompt token, until `steps`
+    positions or a stop token. `engine` has forward.js's members and a bound logits array `engine.bound_logits`.
+    Returns (the blocks fed as (pos, tokens) pairs, the chosen ids)."""
+    fed, calls = [bos] + list(prompt[:-1]), []
+    at = 0
+    while at < len(fed):
+        block = fed[at:at + int(engine.promptBlock)]
+        engine.forwardMany(block, at)
+        calls.append((at, list(block)))
+        at += len(block)
+    token, pos, chosen = prompt[-1], len(fed), []
+    while pos < steps:
+        engine.forward(token, pos)
+        calls.append((pos, [token]))
+        nxt = int(np.argmax(engine.bound_logits))
+        assert np.isfinite(engine.bound_logits[nxt]), "NOT_FINITE"
+        chosen.append(nxt)
+        if nxt in stops:
+            break
+        token, pos = nxt, pos + 1
+    return calls, chosen
+
+
+class OracleAsEngine:
+    """forward.js's members over the oracle (test infrastructure), for generate_like_the_reference."""
+
+    def __init__(self, data, plan, block):
+        self.ref = oracle.OracleEngine(data, plan, half_keys=-1, threads=2)
+        self.promptBlock = block
+        self.bound_logits = np.zeros(plan["vocab_size"], np.float32)
+
+    def forwardMany(self, tokens, pos):
+        self.ref.forward_many(tokens, pos)
+
+    def forward(self, token, pos, needLogits=True):
+        self.bound_logits[:] = self.ref.forward(token, pos)
+
+
+def test_generate_fixture_is_the_oracles():
+    """generate_tiny_gqa.npz was made by the unmodified reference Llama.generate() driving an oracle-backed engine
+    (tests/golden/make_golden.py): the same driving loop restated here, on the oracle, feeds the same blocks and
+    chooses the same ids; and it matches the calls the reference made."""
+    data, plan, _ = golden_model("tiny_gqa")
+    g = np.load(GOLDEN / "generate_tiny_gqa.npz")
+    prompt, steps = [int(t) for t in g["prompt"]], int(g["steps"])
+    calls, chosen = generate_like_the_reference(OracleAsEngine(data, plan, int(g["prompt_block"])), prompt, steps)
+    assert chosen == [int(t) for t in g["ids"]]
+    assert np.array_equal(np.concatenate([[p + i for i in range(len(t))] for p, t in calls]), g["fed_pos"])
+    assert np.array_equal(np.concatenate([t for _, t in calls]), g["fed_tok"])
+    assert len(calls) == int(g["fed_call"].max()) + 1
+
+
+def test_penalize_and_sample_against_the_numpy_sampler():
+    """kernel.ts penalize/sample (restated in the oracle) against the reference's NumPy sampler (Llama.penalize and
+    Llama.sample, public/llama2_numpy.py:1514-1563) on the same logits, temperatures, top-p values and random
+    numbers (tests/golden/sample.npz): penalize the same to the bit (the same float32 operations); sample draws the
+    same token for all but the draws whose random number falls within rounding of a boundary between two tokens (the
+    kernel's exponentials are float32, NumPy's float64)."""
+    g = np.load(GOLDEN / "sample.npz")
+    same = 0
+    for i in range(g["chosen"].size):
+        pen = oracle.penalize(g["logits"][i], g["history"][i][-64:], 1.3)
+        assert np.array_equal(pen.view(np.uint32), g["penalized"][i].view(np.uint32)), i
+        token = oracle.sample(pen, g["temperature"][i], g["topp"][i], g["random"][i])
+        same += int(token == g["chosen"][i])
+    assert same >= 0.99 * g["chosen"].size, same
+
+
+def test_sample_edges():
+    """sample()'s own rules (kernel.ts:801-868): logits whose largest is NaN or +inf give -1; the nucleus of a token
+    far above the rest is that token alone, whatever the random number; without a nucleus (topp 1) the last
+    cumulative step covers random numbers up to 1."""
+    x = np.zeros(50, np.float32)
+    x[7] = np.nan
+    assert oracle.sample(x, 1.0, 0.9, 0.5) == -1
+    x[7] = np.inf
+    assert oracle.sample(x, 1.0, 0.9, 0.5) == -1
+    y = np.zeros(50, np.float32)
+    y[31] = 40.0
+    assert all(oracle.sample(y, 1.0, 0.9, r) == 31 for r in (0.0, 0.5, 0.999999))
+    z = np.zeros(8, np.float32)
+    assert [oracle.sample(z, 1.0, 1.0, r) for r in (0.0, 0.13, 0.99999)] == [0, 1, 7]

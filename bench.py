@@ -58,10 +58,11 @@ def parse():
     p.add_argument("--cpu-prompt", type=int, default=16)
     p.add_argument("--cpu-gen", type=int, default=8)
     p.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "stories15m"])
-    p.add_argument("--config", default="c5", choices=["c5", "c4", "c3"],
+    p.add_argument("--config", default="c5", choices=["c5", "c4", "c3", "c2"],
                    help="c5: the end-to-end line (default); c4: only the int8 matmul sweep over the 8B projection "
                         "shapes at M = 1, 8, 64, 512; c3: only decode attention over 64 sequences with contexts "
-                        "U[512, 8192] (both also part of the c5 line)")
+                        "U[512, 8192]; c2: only causal prefill attention on the tensor cores, 4 x 2048 tokens, 8 heads "
+                        "of 64 (all three also part of the c5 line)")
     p.add_argument("--matmul", default=None, metavar="ROWSxN",
                    help="time the int8 matmul alone (b200k_matmul_q8s) at ROWSxN with --seqs tokens, one matrix of "
                         "random weights on the device: the small case the kernel profiles are captured on")
@@ -361,6 +362,68 @@ def c3_decode_attention(peaks, reps=5):
     return res
 
 
+def c2_prefill_attention(peaks, reps=20):
+    """Causal attention of whole prompts on the tensor cores (b200k_prefill_attention: RoPE + float16 conversion,
+    then the tcgen05 flash-attention kernel): 4 sequences of 2048 tokens, 8 heads = 8 kv heads of 64, RoPE theta
+    1e4, Q/K/V N(0, 1) (seed 1). FLOPs: the causal QK^T and PV, 4 B H d S (S + 1) / 2 = 17.18 G, against the measured
+    dense bf16 tensor rate (the float16 rate is the same)."""
+    import ctypes
+
+    import torch
+
+    from b200fwd import abi
+    from b200fwd import checkpoint as ck
+
+    lib = abi.load()
+    B, S, H, D = 4, 2048, 8, 64
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q, k, v = (torch.randn((B, S, H, D), generator=g, device="cuda") for _ in range(3))
+    cos, sin = ck.rope_tables(S, D, 10000.0)
+    cos_t = torch.from_numpy(np.ascontiguousarray(cos, np.float32)).cuda()
+    sin_t = torch.from_numpy(np.ascontiguousarray(sin, np.float32)).cuda()
+    size = ctypes.c_uint64()
+    abi.check(lib.b200k_prefill_attention_scratch(B, S, H, H, D, ctypes.byref(size)))
+    scratch = torch.empty(int(size.value) + 256, dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(q)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def launch():
+        abi.check(lib.b200k_prefill_attention(ptr(out), ptr(q), ptr(k), ptr(v), ptr(cos_t), ptr(sin_t), B, S, H, H,
+                                              D, ptr(scratch), stream), "prefill_attention")
+
+    for _ in range(3):
+        launch()
+    abi.check(lib.b200k_prefill_attention_check(ptr(scratch), B, S, H, H, D, stream))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        launch()
+    b.record()
+    torch.cuda.synchronize()
+    abi.check(lib.b200k_prefill_attention_check(ptr(scratch), B, S, H, H, D, stream))
+    us = a.elapsed_time(b) * 1e3 / reps
+    flops = 4.0 * B * H * D * S * (S + 1) / 2
+    tf = flops / (us * 1e-6) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    return {"what": "causal prefill attention, 4 x 2048 tokens, 8/8 heads of 64, RoPE 1e4, float16 tensor cores "
+                    "(kind::f16, float32 accumulate), within 1e-3 of float64", "us": us, "flops": flops,
+            "tflops": tf, "tensor_frac": tf / peak, "peak_tflops": peak,
+            "note": "time of the whole call: the RoPE/float16 prologue and the flash-attention kernel"}
+
+
+def c2_arm(args):
+    """bench.py --config c2: prefill attention alone (one GPU)."""
+    import torch
+
+    torch.cuda.set_device(0)
+    peaks, which = measured_peaks()
+    res = c2_prefill_attention(peaks)
+    res["peak_source"] = which
+    print(json.dumps({"config": "c2", **res}), flush=True)
+    return 0
+
+
 def c3_arm(args):
     """bench.py --config c3: decode attention alone (one GPU)."""
     import torch
@@ -509,6 +572,7 @@ def b200_arm(args):
         roof["peak_source"] = which
         c4 = c4_sweep(eng, peaks)
         c3 = c3_decode_attention(peaks)
+        c2 = c2_prefill_attention(peaks)
         cpu_v, cpu_dt, _ = cpu_sample(ckpt_host, plan, args, host_threads())
         # the same oracle on one thread, a shorter sample (4 prompt tokens + 2 greedy steps)
         one = argparse.Namespace(**{**vars(args), "cpu_prompt": 4, "cpu_gen": 2})
@@ -540,6 +604,7 @@ def b200_arm(args):
                                                f"model ({cpu1_dt:.1f} s)"},
             "c4_matmul": c4,
             "c3_decode_attention": c3,
+            "c2_prefill_attention": c2,
             "gpu_launches": launches // max(1, args.steps) * args.steps,
             "clocks": clk,
         }
@@ -606,6 +671,8 @@ def main():
         return c4_arm(args)
     if args.config == "c3":
         return c3_arm(args)
+    if args.config == "c2":
+        return c2_arm(args)
     return b200_arm(args)
 
 

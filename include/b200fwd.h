@@ -249,6 +249,22 @@ int b200k_penalize(float *logits, const int32_t *tokens, int32_t count, float pe
 int b200k_sample(int32_t *out, const float *logits, int32_t n, float temperature, float topp, double random,
                  void *scratch, b200fwd_stream stream);
 int b200k_sample_scratch(int32_t n, uint64_t *bytes);
+/* Causal attention of whole prompts on the tensor cores: what public/forward.js:1055-1057 computes one query token
+ * at a time (kernel.ts:344-357 rope on the query and the keys, then kernel.ts:447-566 attentionOf over positions
+ * 0..t), for every token of `batch` sequences of `seq` tokens at once. q [batch][seq][heads][head_size], k and v
+ * [batch][seq][kv_heads][head_size] float32 (before RoPE; device), the RoPE tables fcr, fci [seq][head_size / 2]
+ * (device); out [batch][seq][heads][head_size] float32. Float16 operands on the tensor cores with float32
+ * accumulation: within 1e-3 of the exact result relative to its largest value (not bit-exact). head_size 64, seq a
+ * multiple of 128. scratch: b200k_prefill_attention_scratch() bytes of device memory, 256-byte aligned. */
+int b200k_prefill_attention(float *out, const float *q, const float *k, const float *v, const float *fcr,
+                            const float *fci, int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads,
+                            int32_t head_size, void *scratch, b200fwd_stream stream);
+int b200k_prefill_attention_scratch(int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads, int32_t head_size,
+                                    uint64_t *bytes);
+/* b200k_prefill_attention only enqueues its kernels; this waits for them and gives B200FWD_ETIMEOUT where one of the
+ * kernel's bounded pipeline waits gave up (the word it leaves in the scratch), else 0. */
+int b200k_prefill_attention_check(const void *scratch, int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads,
+                                  int32_t head_size, b200fwd_stream stream);
 /* kernel.ts:695-699 argmax (first index of the largest, `>`), into *out (device int32). */
 int b200k_argmax(int32_t *out, const float *x, int32_t n, b200fwd_stream stream);
 

@@ -159,6 +159,9 @@ def load():
         "b200k_add_columns": (P, P, P, I32, I32, P),
         "b200k_argmax": (P, P, I32, P),
         "b200k_penalize": (P, P, I32, ctypes.c_float, P),
+        "b200k_prefill_attention": (P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P),
+        "b200k_prefill_attention_scratch": (I32, I32, I32, I32, I32, ctypes.POINTER(U64)),
+        "b200k_prefill_attention_check": (P, I32, I32, I32, I32, I32, P),
         "b200k_sample": (P, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_double, P, P),
         "b200k_sample_scratch": (I32, ctypes.POINTER(U64)),
         "b200fwd_generate_many": (P, I32, P, P, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, P, P,

@@ -1,5 +1,6 @@
 // capi.cu — the kernel entry points of include/b200fwd.h (b200k_*): the exports of kernels/kernel.ts and
 // kernels/kernel_relaxed.ts (public/jobs.js:56-62 lists them), as sm_100a kernels on device pointers.
+#include <cmath>
 #include <string>
 
 #include "common.h"
@@ -219,6 +220,34 @@ int b200k_sample(int32_t *out, const float *logits, int32_t n, float temperature
     int32_t *stack = reinterpret_cast<int32_t *>(probs + sample_scratch_words(n));
     return launch_sample(out, logits, 0, n, temperature, topp, nullptr, random, 0, nullptr, probs, stack, nullptr, 1,
                          as_stream(stream));
+  });
+}
+
+int b200k_prefill_attention_scratch(int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads, int32_t head_size,
+                                    uint64_t *bytes) {
+  if (!bytes || batch < 1 || seq < 1 || heads < 1 || kv_heads < 1 || head_size < 1)
+    return fail(B200FWD_EINVAL, "prefill_attention_scratch: bad arguments");
+  *bytes = prefill_attention_scratch(batch, seq, heads, kv_heads, head_size);
+  return 0;
+}
+
+int b200k_prefill_attention(float *out, const float *q, const float *k, const float *v, const float *fcr,
+                            const float *fci, int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads,
+                            int32_t head_size, void *scratch, b200fwd_stream stream) {
+  return guarded([&] {
+    if (!out || !q || !k || !v || !fcr || !fci || !scratch) return fail(B200FWD_EINVAL, "prefill_attention: null");
+    // kernel.ts:454 isq = 1 / sqrt(hs), in float32
+    const float isq = 1.0f / sqrtf((float)head_size);
+    return launch_prefill_attention(out, q, k, v, fcr, fci, batch, seq, heads, kv_heads, head_size, isq, scratch,
+                                    as_stream(stream));
+  });
+}
+
+int b200k_prefill_attention_check(const void *scratch, int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads,
+                                  int32_t head_size, b200fwd_stream stream) {
+  return guarded([&] {
+    if (!scratch) return fail(B200FWD_EINVAL, "prefill_attention_check: null scratch");
+    return check_prefill_attention(scratch, batch, seq, heads, kv_heads, head_size, as_stream(stream));
   });
 }
 

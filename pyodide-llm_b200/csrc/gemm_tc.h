@@ -24,6 +24,9 @@ struct GemmMaps {
   CUtensorMap xs;  // float32 activation scales [groups][stride >= tokens], one row per group: boxes of bn x 4
 };
 
+// a 2-D TMA map: cols elements of esize bytes per row, rows rows row_bytes apart, boxes of box_cols x box_rows
+int make_map(CUtensorMap *map, CUtensorMapDataType type, int esize, const void *base, int64_t cols, int64_t rows,
+             int64_t row_bytes, int box_cols, int box_rows, CUtensorMapSwizzle swizzle);
 // int8 rows: cols bytes of rows rows, row_bytes apart; boxes of 128 bytes x box_rows rows, 128-byte swizzle (the
 // layout the tcgen05 descriptors of gemm_tc.cu read)
 int make_i8_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t row_bytes, int box_rows);

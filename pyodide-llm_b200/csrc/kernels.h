@@ -112,6 +112,14 @@ int launch_advance_sampled(int32_t *tokens, int32_t *pos, const int32_t *ids, in
                            int32_t *step, int count, const float *logits, int64_t vocab, int greedy, int32_t *recent,
                            int window, int32_t *recent_count, const int32_t *stops, int nstops, int32_t *done,
                            int32_t *made, int32_t *bad, cudaStream_t stream);
+// causal attention of whole sequences on the tensor cores (attention_tc.cu): q [B][S][H][D], k and v [B][S][KV][D]
+// float32, RoPE tables [S][D/2]; out [B][S][H][D]; scratch prefill_attention_scratch() bytes (256-byte aligned)
+size_t prefill_attention_scratch(int B, int S, int H, int KV, int D);
+int launch_prefill_attention(float *out, const float *q, const float *k, const float *v, const float *cos_t,
+                             const float *sin_t, int B, int S, int H, int KV, int D, float scale, void *scratch,
+                             cudaStream_t stream);
+// after the kernel: its pipeline-wait error word (in the scratch) as a status (synchronizes the stream)
+int check_prefill_attention(const void *scratch, int B, int S, int H, int KV, int D, cudaStream_t stream);
 // kernel.ts:330-342 rmsnorm of count rows (stride floats apart)
 int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps, int count, int64_t stride,
                    cudaStream_t stream);

@@ -255,7 +255,7 @@ int b200k_sample_scratch(int32_t n, uint64_t *bytes);
  * [batch][seq][kv_heads][head_size] float32 (before RoPE; device), the RoPE tables fcr, fci [seq][head_size / 2]
  * (device); out [batch][seq][heads][head_size] float32. Float16 operands on the tensor cores with float32
  * accumulation: within 1e-3 of the exact result relative to its largest value (not bit-exact). head_size 64, seq a
- * multiple of 128. scratch: b200k_prefill_attention_scratch() bytes of device memory, 256-byte aligned. */
+ * multiple of 256. scratch: b200k_prefill_attention_scratch() bytes of device memory, 256-byte aligned. */
 int b200k_prefill_attention(float *out, const float *q, const float *k, const float *v, const float *fcr,
                             const float *fci, int32_t batch, int32_t seq, int32_t heads, int32_t kv_heads,
                             int32_t head_size, void *scratch, b200fwd_stream stream);

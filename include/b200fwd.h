@@ -199,7 +199,9 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
                      const int32_t *wc, int32_t n, int32_t r0, int32_t r1, int32_t count, int64_t out_stride,
                      int64_t q_stride, int64_t s_stride, b200fwd_stream stream);
 /* kernel_relaxed.ts:34-67 / 164-183 on activations already less the bias (xq[i] = q[i] - 64, signed; the engine
- * keeps them so): all `rows` rows of W for `count` tokens, the same numbers to the bit. From 16 tokens on (with
+ * keeps them so): all `rows` rows of W for `count` tokens, the same numbers to the bit. The tensor-core path reports
+ * a pipeline wait that gave up through one device word of the library's: calls that overlap on the GPU (other
+ * streams or threads) share it and must be serialized. From 16 tokens on (with
  * n >= 128, rows >= 128, and ws_stride a multiple of 4 floats: TMA rows of whole 16 bytes) it runs on the tensor
  * cores (tcgen05.mma kind::i8, one MMA per group of 32), else on the CUDA cores. ws: row r's scales at
  * ws + r * ws_stride (0: n / 32). xq, wq, ws 16-byte aligned; q_stride a multiple of 16. */
@@ -225,9 +227,10 @@ int b200k_attention(float *out, const float *q, const void *kc, const void *vc, 
  * (inside a stream capture, where cudaMalloc is not allowed; on a latency path that must not stall the device the
  * way cudaMalloc can; under a fixed device budget): the same numbers, with the softmax scratch in a 4 MiB array of
  * the library's own, which every GPU that loads the library holds until exit. nh * (pos + 1) may be at most
- * 1048576 (else B200FWD_EINVAL). The first call on a device looks the array up, so make it before any capture.
- * Every call shares the array: calls that overlap on the GPU race. Nothing needs zeroing; it keeps the last
- * call's softmax weights. */
+ * 1048576 and pos + 1 at most 51200 (else B200FWD_EINVAL). The first call on a device looks the array up, so make it
+ * before any capture; the address is kept for the process's life, so do not call it again after a
+ * cudaDeviceReset. Every call shares the array: calls that overlap on the GPU race. Nothing needs zeroing; it keeps
+ * the last call's softmax weights. */
 int b200k_attention_static(float *out, const float *q, const void *kc, const void *vc, int32_t pos, int32_t nh,
                            int32_t nkv, int32_t hs, int32_t h0, int32_t h1, int32_t half, b200fwd_stream stream);
 /* kernel.ts:570-599 to_f16 (round to nearest even, NumPy's astype(float16)) and kernel.ts:604-608 from_f16. */

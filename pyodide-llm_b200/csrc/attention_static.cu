@@ -14,7 +14,10 @@
 //    serialize them;
 //  - nothing in the array must start at zero (each call writes every weight it reads first), and it keeps the last
 //    call's weights afterwards;
-//  - nh * (pos + 1) above STATIC_SCRATCH_FLOATS is refused with B200FWD_EINVAL.
+//  - nh * (pos + 1) above STATIC_SCRATCH_FLOATS is refused with B200FWD_EINVAL, and so is pos + 1 above
+//    MAX_POSITIONS (51200: the softmax of one head holds a row of weights in a block's shared memory);
+//  - the array's address is kept for the life of the process: a host that calls cudaDeviceReset after using this
+//    entry must not call it again in that process (the address it kept may no longer be the array's).
 #include <mutex>
 #include <string>
 
@@ -24,6 +27,7 @@
 namespace {
 
 constexpr int64_t STATIC_SCRATCH_FLOATS = 1 << 20;  // 4 MiB: e.g. 32 heads at 32768 positions
+constexpr int64_t MAX_POSITIONS = 51200;             // 200 KiB of one block's shared memory, 4 bytes a weight
 
 // the scratch, one per device; its name in host code is not a device address (see scratch_on_current_device)
 static __device__ __align__(256) float static_scratch[STATIC_SCRATCH_FLOATS];
@@ -57,8 +61,12 @@ extern "C" int b200k_attention_static(float *out, const float *q, const void *kc
     if (!out || !q || !kc || !vc) return b200::fail(B200FWD_EINVAL, "attention_static: null pointer");
     if (pos < 0 || nh < 1 || nkv < 1 || nh % nkv || hs < 1 || h0 < 0 || h1 > nh || h0 > h1)
       return b200::fail(B200FWD_EINVAL, "attention_static: bad sizes");
-    if ((int64_t)nh * (pos + 1) > STATIC_SCRATCH_FLOATS)
-      return b200::fail(B200FWD_EINVAL, "attention_static: nh * (pos + 1) = " + std::to_string((int64_t)nh * (pos + 1)) +
+    const int64_t count = (int64_t)pos + 1;
+    if (count > MAX_POSITIONS)
+      return b200::fail(B200FWD_EINVAL, "attention_static: pos + 1 = " + std::to_string(count) + " positions, above " +
+                                            std::to_string(MAX_POSITIONS) + " (a softmax row in one block)");
+    if ((int64_t)nh * count > STATIC_SCRATCH_FLOATS)
+      return b200::fail(B200FWD_EINVAL, "attention_static: nh * (pos + 1) = " + std::to_string((int64_t)nh * count) +
                                             " floats of scratch, above this entry's fixed " +
                                             std::to_string(STATIC_SCRATCH_FLOATS) +
                                             " (use b200k_attention with scratch of your own)");

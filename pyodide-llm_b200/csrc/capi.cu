@@ -104,6 +104,8 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
       cudaStream_t s;
       ~Free() { cudaFreeAsync(p, s); }
     } free_xs{xs_g, st};
+    // the error word starts this call at 0, in stream order (calls that overlap on the GPU share it: see the header)
+    B200_CUDA(cudaMemsetAsync(err, 0, 4, st));
     int rc = launch_scales_by_group(xs_g, tstride, xs, s_stride, count, n / 32, st);
     GemmMaps maps;
     if (!rc) rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
@@ -125,11 +127,7 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     int32_t e = 0;
     B200_CUDA(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, st));
     B200_CUDA(cudaStreamSynchronize(st));
-    if (e) {
-      const int32_t zero = 0;
-      B200_CUDA(cudaMemcpy(err, &zero, 4, cudaMemcpyHostToDevice));
-      return fail(B200FWD_ETIMEOUT, "matmul_q8s: a tensor-core pipeline wait gave up (code " + std::to_string(e) + ")");
-    }
+    if (e) return fail(B200FWD_ETIMEOUT, "matmul_q8s: a tensor-core pipeline wait gave up (code " + std::to_string(e) + ")");
     return 0;
   });
 }

@@ -49,3 +49,6 @@ def test_no_alloc_attention_refuses_past_its_array():
     q = full(32 * 128, 0.0)
     rc = lib.b200k_attention_static(ptr(q), ptr(q), ptr(q), ptr(q), 40000, 32, 8, 128, 0, 32, 1, None)
     assert rc == abi.EINVAL and "1048576" in abi.last_error()
+    # one head of 60000 positions fits the array but not one softmax row of a block: refused before any launch
+    rc = lib.b200k_attention_static(ptr(q), ptr(q), ptr(q), ptr(q), 59999, 1, 1, 128, 0, 1, 1, None)
+    assert rc == abi.EINVAL and "51200" in abi.last_error()

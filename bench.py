@@ -305,7 +305,7 @@ def c4_sweep(eng, peaks, counts=(1, 8, 64, 512), reps=2):
             row[shape] = e
         out[f"M={m}"] = row
     return {"what": "int8 group-32 matmul (exact order) per launch, every layer's copy in turn (no L2 hits)",
-            "kernel": "matvec_kernel (CUDA cores) below 16 tokens, q8_gemm_tc (tcgen05) from 16",
+            "kernel": "matvec_kernel (CUDA cores) for one token, q8_gemm_tc (tcgen05) from 2",
             "peak_hbm_gbs": hbm, "int8_tops_peak": int8_tops, "table": out}
 
 

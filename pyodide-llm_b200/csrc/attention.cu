@@ -15,9 +15,9 @@
 //           fours one by one (kernel.ts:522-565); values past the fours of a head add their four products one after
 //           another.
 //
-// Single query tokens (decode; the whole-head rows 16-byte aligned) take attn_scores_decode / attn_values_decode
-// instead: key chunks of DEC_POS positions and value chunks of VCH positions come to shared memory by cp.async
-// (the values VNB - 1 chunks ahead, with their softmax weights), are widened once per block, and the lane sums and
+// Single query tokens (decode; the whole-head rows 16-byte aligned) take attn_scores_decode and, for float16 caches
+// with heads of a multiple of 64 values, attn_values_decode_h (else attn_values_decode) instead: key chunks of
+// DEC_POS positions and value chunks come to shared memory by cp.async several chunks ahead, and the lane sums and
 // the fours of positions run on paired float32 operations (fma with a run-time one for the adds, so that every
 // product and sum keeps the reference's own rounding).
 #include <algorithm>
@@ -501,6 +501,123 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
+constexpr int HCH = 32;  // positions of a value chunk (attn_values_decode_h)
+constexpr int HNB = 6;   // value chunks in flight
+
+// the reference's half() of two float16 values (kernel.ts half: bits << 13 with the sign kept, times 2^112), less the
+// factor 2^112: the float32 whose bits are the half's shifted into place. The caller multiplies the weights by 2^112
+// instead: w * 2^112 is exact (a power of two; the weights lie in [0, 1]) and the product with the shifted bits is
+// the same real number as w * half(v), so it rounds to the same float.
+__device__ __forceinline__ uint64_t half2_bits(uint32_t u) {
+  const uint32_t lo = (uint32_t)((int32_t)(u << 16) >> 3) & 0x8fffe000u;
+  const uint32_t hi = (uint32_t)((int32_t)u >> 3) & 0x8fffe000u;
+  return (uint64_t)lo | ((uint64_t)hi << 32);
+}
+
+// Decode values over a float16 cache, heads a multiple of 64 values: grid (kv heads x hs / 64, tokens), one warp a
+// block; lane l takes the values dim0 + 2l and dim0 + 2l + 1 (dim0 = 64 x the block's part) of all G query heads of
+// the kv head, so every float16 pair is widened once for G heads. The same chain as attn_values_tiled: per head and
+// value the positions in fours ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) added in order, then the positions past the fours
+// one by one (kernel.ts:522-565). The values come in chunks of HCH positions by cp.async, HNB - 1 chunks ahead; the
+// chunk's weights (times 2^112, each twice for the paired multiplies) are read one chunk ahead into registers and
+// stored to shared memory after the chunk before is done.
+template <int G>
+__global__ void __launch_bounds__(32)
+    attn_values_decode_h(float *out, int64_t out_stride, const uint16_t *vc, const float *att, const int32_t *seq,
+                         const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
+                         int h1, float one) {
+  __shared__ __align__(16) uint32_t vbuf[HNB][HCH][32];  // raw float16 pairs: [chunk][position][lane]
+  __shared__ __align__(16) uint64_t wbuf[2][G][HCH];     // the weights x 2^112, twice: [chunk & 1][head][position]
+  const int parts = hs >> 6;
+  const int kvh = blockIdx.x / parts, dim0 = (blockIdx.x % parts) * 64, tok = blockIdx.y;
+  const int lane = threadIdx.x;
+  const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
+  const int chunks = (count + HCH - 1) / HCH;
+  const int64_t kvDim = (int64_t)nkv * hs;
+  const uint16_t *vbase = vc + (seq ? (int64_t)seq[tok] : 0) * seq_stride + (int64_t)kvh * hs + dim0;
+  const float *watt = att + ((int64_t)tok * nh + (int64_t)kvh * G) * P;  // head kvh * G + g's row at g * P
+  const float big = 5.192296858534828e33f;                                // 2^112
+  // chunk c's values into buffer c % HNB: 16-byte piece lane % 8 of the rows lane / 8 + 4 i (one commit group per
+  // call, empty past the last chunk)
+  auto issue = [&](int c) {
+    if (c < chunks) {
+      const int r0 = c * HCH, rows = min(HCH, count - r0);
+      uint32_t(*dst)[32] = vbuf[c % HNB];
+      const int piece = lane & 7;
+#pragma unroll
+      for (int i = 0; i < HCH / 4; i++) {
+        const int r = (lane >> 3) + 4 * i;
+        if (r < rows) cp_async16(&dst[r][4 * piece], vbase + (int64_t)(r0 + r) * kvDim + 8 * piece);
+      }
+    }
+    cp_async_commit();
+  };
+  auto load_weights = [&](int c, float (&w)[G]) {
+    const int p = c * HCH + lane;
+#pragma unroll
+    for (int g = 0; g < G; g++) w[g] = c < chunks && p < count ? watt[(int64_t)g * P + p] : 0.0f;
+  };
+  auto store_weights = [&](int c, const float (&w)[G]) {
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const float s = fmul(w[g], big);
+      wbuf[c & 1][g][lane] = pk(s, s);
+    }
+  };
+  const uint64_t one2 = pk(one, one);
+  uint64_t o[G];
+#pragma unroll
+  for (int g = 0; g < G; g++) o[g] = 0;
+  for (int c = 0; c + 1 < HNB; c++) issue(c);
+  {
+    float w[G];
+    load_weights(0, w);
+    store_weights(0, w);
+  }
+  for (int c = 0; c < chunks; c++) {
+    issue(c + HNB - 1);
+    float wn[G];
+    load_weights(c + 1, wn);
+    cp_async_wait<HNB - 1>();
+    __syncwarp();  // chunk c's values (every lane's copies) and weights are in shared memory
+    const uint32_t(*vb)[32] = vbuf[c % HNB];
+    const uint64_t(*wb)[HCH] = wbuf[c & 1];
+    const int r0 = c * HCH, rows = min(HCH, count - r0);
+    const int rows4 = max(0, min(rows, count4 - r0));  // a multiple of four (r0 is)
+#pragma unroll 2
+    for (int i = 0; i < rows4; i += 4) {
+      const uint64_t v0 = half2_bits(vb[i][lane]), v1 = half2_bits(vb[i + 1][lane]);
+      const uint64_t v2 = half2_bits(vb[i + 2][lane]), v3 = half2_bits(vb[i + 3][lane]);
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const ulonglong2 w01 = *reinterpret_cast<const ulonglong2 *>(&wb[g][i]);
+        const ulonglong2 w23 = *reinterpret_cast<const ulonglong2 *>(&wb[g][i + 2]);
+        const uint64_t s01 = fma2(one2, mul2(w01.x, v0), mul2(w01.y, v1));
+        const uint64_t s23 = fma2(one2, mul2(w23.x, v2), mul2(w23.y, v3));
+        o[g] = fma2(one2, o[g], fma2(one2, s01, s23));
+      }
+    }
+    // the positions past the fours, one at a time (kernel.ts:548-564)
+    for (int i = rows4; i < rows; i++) {
+      const uint64_t v = half2_bits(vb[i][lane]);
+#pragma unroll
+      for (int g = 0; g < G; g++) o[g] = fma2(one2, o[g], mul2(wb[g][i], v));
+    }
+    // chunk c + 1's weights into the buffer chunk c - 1's used; then every lane is done with chunk c (its values'
+    // buffer is the next one refilled) and the weights are in place
+    store_weights(c + 1, wn);
+    __syncwarp();
+  }
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    const int h = kvh * G + g;
+    if (h < h0 || h >= h1) continue;
+    float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + dim0 + 2 * lane;
+    dst[0] = lo(o[g]);
+    dst[1] = hi(o[g]);
+  }
+}
+
 template <bool HALF, int G>
 int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                  float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
@@ -529,6 +646,13 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
       const int c = v ? atoi(v) : 0;
       return c == 1 || c == 2 || c == 4 || c == 8 ? c : 2;
     }();
+    if (HALF && hs % 64 == 0) {
+      attn_values_decode_h<G><<<dim3(nkv * (hs / 64), count), 32, 0, stream>>>(
+          out, out_stride, static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
+          1.0f);
+      B200_LAUNCHED("attn_values_decode_h");
+      return 0;
+    }
     int parts = 1;
     for (int p = cap; p > 1; p /= 2) {
       const int dims = hs / p;

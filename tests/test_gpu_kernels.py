@@ -239,6 +239,25 @@ def test_attention_shapes(lib, nh, nkv, hs, half):
         assert np.array_equal(bits(both), bits(ref)), pos
 
 
+@pytest.mark.parametrize("hs", [64, 128])
+def test_attention_half_values_of_every_bit_pattern(lib, hs):
+    """Float16 value caches of arbitrary bit patterns (subnormals, zeros of both signs, the top exponent that the
+    reference's half() widens to finite numbers) through the decode kernels, to the bit against the oracle: the
+    values kernel folds half()'s 2^112 into the weights."""
+    rng = np.random.default_rng(hs)
+    nh, nkv = 32, 8
+    for pos in (2, 3, 130, 301):
+        count = pos + 1
+        q = rng.standard_normal(nh * hs).astype(np.float32)
+        kc = oracle.to_f16((rng.standard_normal((count, nkv * hs)) * 0.05).astype(np.float32)).reshape(count, -1)
+        vc = rng.integers(0, 65536, (count, nkv * hs)).astype(np.uint16)
+        vc[0, :8] = [0x0000, 0x8000, 0x0001, 0x83ff, 0x7c00, 0xfc00, 0x7e01, 0x7bff]
+        got, att = attention_gpu(lib, q, kc, vc, pos, nh, nkv, hs, True)
+        ref, ref_att = oracle.attention(q, kc, vc, pos, nh, nkv, hs, half=True)
+        assert np.array_equal(bits(att), bits(ref_att)), pos
+        assert np.array_equal(bits(got), bits(ref)), pos
+
+
 def test_attention_batch_is_per_token(lib):
     """b200k_attention_batch: each token against its own sequence's cache gives b200k_attention's numbers."""
     rng = np.random.default_rng(9)

@@ -107,12 +107,6 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     // the error word starts this call at 0, in stream order (calls that overlap on the GPU share it: see the header)
     B200_CUDA(cudaMemsetAsync(err, 0, 4, st));
     int rc = launch_scales_by_group(xs_g, tstride, xs, s_stride, count, n / 32, st);
-    GemmMaps maps;
-    if (!rc) rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
-    if (!rc) rc = make_i8_map(&maps.x, xq, n, count, q_stride, bn);
-    if (!rc) rc = make_scale_map(&maps.ws, ws, ws_stride, rows, ws_stride, 128);
-    if (!rc) rc = make_token_scale_map(&maps.xs, xs_g, count, n / 32, tstride, bn);
-    if (rc) return rc;
     GemmArgs a{};
     a.out = xout;
     a.error = err;
@@ -122,7 +116,20 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     a.w_row0 = 0;
     a.out_stride = out_stride;
     a.accumulate = 0;
-    rc = launch_gemm_tc(maps, a, bn, st);
+    GemmMaps maps;
+    if (!rc && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) && gemm_lanes_pays(rows, count, sms)) {
+      // n a multiple of 128 and few row tiles: the lane-split kernel (a cluster of four CTAs per tile)
+      const int lbn = choose_lanes_bn(count, count >= 64 ? 64 : count >= 32 ? 32 : 16);
+      rc = make_lane_weight_maps(&maps.w, &maps.ws, wq, ws, n, rows, ws_stride);
+      if (!rc) rc = make_lane_token_maps(&maps.x, &maps.xs, xq, xs_g, count, q_stride, n, tstride, lbn);
+      if (!rc) rc = launch_gemm_lanes(maps, a, lbn, st);
+    } else {
+      if (!rc) rc = make_i8_map(&maps.w, wq, n, rows, n, 128);
+      if (!rc) rc = make_i8_map(&maps.x, xq, n, count, q_stride, bn);
+      if (!rc) rc = make_scale_map(&maps.ws, ws, ws_stride, rows, ws_stride, 128);
+      if (!rc) rc = make_token_scale_map(&maps.xs, xs_g, count, n / 32, tstride, bn);
+      if (!rc) rc = launch_gemm_tc(maps, a, bn, st);
+    }
     if (rc) return rc;
     int32_t e = 0;
     B200_CUDA(cudaMemcpyAsync(&e, err, 4, cudaMemcpyDeviceToHost, st));

@@ -48,8 +48,9 @@ struct Matrix {
   int8_t *w = nullptr;
   float *s = nullptr;
   int rows = 0, n = 0, layers = 1, sstride = 0;
-  bool mapped = false;
+  bool mapped = false, lane_mapped = false;
   CUtensorMap wmap, smap;
+  CUtensorMap lwmap, lsmap;  // the lane-split matmul's (gemm_lanes.cu)
   const int8_t *layer_w(int l) const { return w + (int64_t)l * rows * n; }
   const float *layer_s(int l) const { return s + (int64_t)l * rows * sstride; }
 };
@@ -102,6 +103,8 @@ struct b200fwd_engine {
   int32_t *meta = nullptr;      // device: tokens[T], seq[T], pos[T], want[T], step, bad, tc error, -, tiles[2T]
   CUtensorMap xmap[3], xsmap[3]; // the activations and their scales, for tiles of 16, 32 and 64 tokens
   int widest_tile = 0;           // the widest of those tiles the activations have room for
+  CUtensorMap lxmap[3], lxsmap[3];  // the same for the lane-split matmul
+  bool lanes = false;
   bool tensor_cores = true;
   int sms = 148;
   int32_t *meta_h = nullptr;    // pinned host copy
@@ -273,6 +276,12 @@ int alloc_activations(b200fwd_engine *e) {
       CHECK(make_token_scale_map(&e->xsmap[i], e->xs, T, e->XQ / 32, e->TP, bn));
       e->widest_tile = bn;
     }
+  e->lanes = e->tensor_cores && e->widest_tile == 64 && e->XQ % 128 == 0 && e->XQ >= 2048 && gemm_lanes_enabled();
+  if (e->lanes) {
+    for (int i = 0, bn = 16; i < 3; i++, bn *= 2)
+      CHECK(make_lane_token_maps(&e->lxmap[i], &e->lxsmap[i], e->xq, e->xs, T, e->XQ, e->XQ, e->TP, bn));
+    CHECK(prepare_gemm_lanes());
+  }
   return 0;
 }
 
@@ -326,6 +335,12 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
     a.w_row0 = layer * m.rows;
     a.out_stride = out_stride;
     a.accumulate = accumulate;
+    if (e->lanes && m.lane_mapped && gemm_lanes_fits(m.n, m.rows, count) && gemm_lanes_pays(m.rows, count, e->sms)) {
+      const int bn = choose_lanes_bn(count, 64);
+      const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
+      GemmMaps maps{m.lwmap, e->lxmap[which], m.lsmap, e->lxsmap[which]};
+      return launch_gemm_lanes(maps, a, bn, e->stream);
+    }
     const int bn = choose_gemm_bn(m.rows, count, e->sms, e->widest_tile);
     const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
     GemmMaps maps{m.wmap, e->xmap[which], m.smap, e->xsmap[which]};
@@ -516,6 +531,11 @@ int make_engine(const void *checkpoint, size_t size, const b200fwd_plan *plan, c
       CHECK(make_i8_map(&m->wmap, m->w, m->n, (int64_t)m->layers * m->rows, m->n, 128));
       CHECK(make_scale_map(&m->smap, m->s, m->sstride, (int64_t)m->layers * m->rows, m->sstride, 128));
       m->mapped = true;
+      if (gemm_lanes_enabled() && gemm_lanes_fits(m->n, (int)std::min<int64_t>((int64_t)m->layers * m->rows, 1 << 30), 1)) {
+        CHECK(make_lane_weight_maps(&m->lwmap, &m->lsmap, m->w, m->s, m->n, (int64_t)m->layers * m->rows,
+                                    m->sstride));
+        m->lane_mapped = true;
+      }
     }
 
   if (e->emb.rows != e->vocab || e->emb.n != e->dim || e->wcls.rows != e->vocab || e->wcls.n != e->dim)

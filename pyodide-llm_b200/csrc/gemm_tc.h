@@ -47,4 +47,23 @@ int gemm_sms();
 int prepare_gemm();
 size_t gemm_smem_bytes();
 
+// ---- the lane-split matmul (gemm_lanes.cu): a cluster of four CTAs per tile, one per chain lane; for n a multiple
+// of 128 with at least 16 quads (four stages a tile). Its maps (GemmMaps, other geometry):
+// weights [rows][n] int8 and their scales [rows][sstride] (sstride a multiple of 4)
+int make_lane_weight_maps(CUtensorMap *wmap, CUtensorMap *smap, const void *w, const float *s, int64_t n,
+                          int64_t rows, int64_t sstride);
+// activations [tokens][row_bytes] (k bytes used) and their scales [k / 32][tp] (one row per group), for tiles of bn
+int make_lane_token_maps(CUtensorMap *xmap, CUtensorMap *xsmap, const int8_t *xq, const float *xs, int64_t tokens,
+                         int64_t row_bytes, int64_t k, int64_t tp, int bn);
+bool gemm_lanes_fits(int n, int rows, int count);
+// whether the lane split is the faster kernel for rows x count on `sms` SMs (few row tiles)
+bool gemm_lanes_pays(int rows, int count, int sms);
+// the tile width for count tokens: one tile up to 64 tokens, else tiles of 64; at most `widest` (16, 32 or 64: the
+// token maps' boxes must fit their tensors)
+int choose_lanes_bn(int count, int widest);
+// false when B200FWD_GEMM_LANES=0 (a measurement knob: the one-CTA kernel for every shape)
+bool gemm_lanes_enabled();
+int prepare_gemm_lanes();
+int launch_gemm_lanes(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream);
+
 }  // namespace b200

@@ -176,25 +176,42 @@ __device__ __forceinline__ void quantize_group(float v, int lane, int bias, int8
 
 // kernel.ts:330-342 rmsnorm's scale: four lane chains over the fours, ((0+1)+2)+3, the rest one by one. The whole
 // block squares the vector into shared memory (sq: n floats, each square rounded once as the reference rounds it),
-// then four threads run the lane chains (the chains' adds are the only serial part).
+// then four lanes of warp 0 run the lane chains (the chains' adds are the only serial part: each lane reads its next
+// sixteen squares while it adds the sixteen before, so the adds follow one another at the add's latency).
 constexpr int NORM_MAX = 12288;  // the longest vector a block normalizes (its squares fill 48 KB of shared memory)
 __device__ __forceinline__ float norm_scale(const float *x, int n, float eps, float *sq, float *part) {
-  for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    const float v = x[j];
-    sq[j] = fmul(v, v);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && n % 4 == 0) {
+    for (int j = threadIdx.x; j < n / 4; j += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4 *>(x)[j];
+      reinterpret_cast<float4 *>(sq)[j] = make_float4(fmul(v.x, v.x), fmul(v.y, v.y), fmul(v.z, v.z), fmul(v.w, v.w));
+    }
+  } else {
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      const float v = x[j];
+      sq[j] = fmul(v, v);
+    }
   }
   __syncthreads();
   const int n4 = n & ~3;
   if (threadIdx.x < 4) {
-    // sixteen squares read ahead of their adds (the reads do not wait on the chain)
     float acc = 0.0f;
     int j = threadIdx.x;
-    for (; j + 60 < n4; j += 64) {
-      float v[16];
+    if (j + 60 < n4) {
+      float cur[16];
 #pragma unroll
-      for (int u = 0; u < 16; u++) v[u] = sq[j + 4 * u];
+      for (int u = 0; u < 16; u++) cur[u] = sq[j + 4 * u];
+      for (; j + 124 < n4; j += 64) {
+        float nxt[16];
 #pragma unroll
-      for (int u = 0; u < 16; u++) acc = fadd(acc, v[u]);
+        for (int u = 0; u < 16; u++) nxt[u] = sq[j + 64 + 4 * u];
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) cur[u] = nxt[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+      j += 64;
     }
     for (; j < n4; j += 4) acc = fadd(acc, sq[j]);
     part[threadIdx.x] = acc;
@@ -253,32 +270,30 @@ __global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh
   base[1] = fadd(fmul(v0, s), fmul(v1, c));
 }
 
+// grid (groups / 8 rounded up, tokens): a warp a group of 32
 __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq,
                                 int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
   const int lane = threadIdx.x & 31;
-  const int ng = n >> 5;
-  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= (int64_t)ng * count) return;
-  const int tok = (int)(gw / ng), g = (int)(gw % ng);
+  const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), tok = blockIdx.y;
+  if (g >= (n >> 5)) return;
   const float v = x[(int64_t)tok * x_stride + g * 32 + lane];
   quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
-                   xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+                 xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
-// kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x
+// kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x; grid as quantize_kernel's
 __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int count,
                                        int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
   const int lane = threadIdx.x & 31;
-  const int ng = n >> 5, n4 = n & ~3;
-  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= (int64_t)ng * count) return;
-  const int tok = (int)(gw / ng), g = (int)(gw % ng);
+  const int n4 = n & ~3;
+  const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), tok = blockIdx.y;
+  if (g >= (n >> 5)) return;
   const int j = g * 32 + lane;
   const float v = h1[(int64_t)tok * stride + j];
   const float e = j < n4 ? vexp(-v) : fexp(-v);
   const float o = fmul(fdiv(v, fadd(1.0f, e)), h3[(int64_t)tok * stride + j]);
   quantize_group(o, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
-                   xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+                 xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
@@ -515,10 +530,12 @@ int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "rmsnorm+quantize: n must be whole groups of 32");
   if (n > NORM_MAX) return fail(B200FWD_EUNSUPPORTED, "rmsnorm+quantize: vectors above 12288 values");
-  // a block per token, 32 warps: the squares and the groups' quantization spread over the whole block (only the four
-  // lane chains of the norm are serial)
-  norm_quantize_kernel<<<count, 1024, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs, s_stride, g_stride,
-                                                  channels, nch, picked, out_f, out_stride, shift);
+  // a block per token: the squares and the groups' quantization spread over the block (only the four lane chains of
+  // the norm are serial); 1024 threads while the tokens leave SMs free, 256 (more tokens' chains at once) past that
+  const int threads = count <= 148 ? 1024 : 256;
+  norm_quantize_kernel<<<count, threads, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs,
+                                                                  s_stride, g_stride, channels, nch, picked, out_f,
+                                                                  out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;
 }
@@ -527,9 +544,9 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
                     float *xs, int64_t s_stride, int64_t g_stride, cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "quantize_x: n must be whole groups of 32");
-  const int64_t warps = (int64_t)(n / 32) * count;
-  quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride, xs, s_stride,
-                                                            g_stride, shift);
+  if (count > 65535) return fail(B200FWD_EINVAL, "quantize_x: more than 65535 tokens");
+  quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride,
+                                                                          xs, s_stride, g_stride, shift);
   B200_LAUNCHED("quantize_kernel");
   return 0;
 }
@@ -539,9 +556,10 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
                            cudaStream_t stream, int shift) {
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
-  const int64_t warps = (int64_t)(n / 32) * count;
-  swiglu_quantize_kernel<<<blocks_for(warps, 8), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq, q_stride, xs,
-                                                                   s_stride, g_stride, shift);
+  if (count > 65535) return fail(B200FWD_EINVAL, "swiglu+quantize: more than 65535 tokens");
+  swiglu_quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq,
+                                                                                 q_stride, xs, s_stride, g_stride,
+                                                                                 shift);
   B200_LAUNCHED("swiglu_quantize_kernel");
   return 0;
 }

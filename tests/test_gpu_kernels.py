@@ -155,6 +155,37 @@ def test_matmul_tensor_cores(lib, n, rows, pad):
         assert np.array_equal(bits(got), bits(want[:count])), count
 
 
+@pytest.mark.parametrize("n,rows", [(4096, 256), (4096, 6144), (288, 256)])
+def test_matmul_tensor_cores_extreme_scales(lib, n, rows):
+    """Activation scales from subnormal (6e-39) to 1e29 and weight scales from 1e-32 to 1e18, through both
+    tensor-core kernels (the lane split for 256 rows, the one-CTA kernel for 6144 and for 9 groups), to the bit
+    against the oracle: subnormal scale products, products that underflow, and sums that overflow to infinity. Where
+    an infinity meets one of the other sign the result is NaN on both sides; its bit pattern is the platform's (the
+    GPU's canonical NaN, x86's default NaN; WASM leaves it unspecified), so NaNs are compared as NaNs. (Scales below
+    about 3e-39 have no finite inverse: the reference then quantizes to -128, which the engine's activations less the
+    bias of 64 do not hold; such groups are left out here.)"""
+    rng = np.random.default_rng(n + 7 * rows)
+    w = rng.integers(-128, 128, size=rows * n, dtype=np.int8)
+    ws = rng.uniform(0.001, 0.02, rows * n // 32).astype(np.float32)
+    ws.reshape(rows, -1)[::7] *= np.float32(1e-30)
+    ws.reshape(rows, -1)[3::11] *= np.float32(1e20)
+    wc = oracle.int8_sums(w)
+    count = 64
+    mags = np.array([3e-37, 1e-36, 1e-31, 1e-20, 1.0, 1e20, 1e30, 6e-37], np.float32)
+    x = rng.standard_normal((count, n)).astype(np.float32) * mags[np.arange(count) % len(mags)][:, None]
+    xq = np.zeros((count, n), np.int8)
+    xs = np.zeros((count, n // 32), np.float32)
+    for t in range(count):
+        xq[t], xs[t] = oracle.quantize_x(x[t], 64)
+    assert (xs[xs > 0] < np.float32(1.2e-38)).any() and (xq != -128).all()  # subnormal scales among them
+    got = matmul_signed(lib, xq, xs, w, ws, n, count, 4)
+    want = np.stack([oracle.matmul_q8r(xq[t], xs[t], w, ws, wc, n) for t in range(count)])
+    assert np.isnan(want).any() and (np.abs(want) < np.float32(1.2e-38)).any()  # both ends reached
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    finite = ~np.isnan(want)
+    assert np.array_equal(bits(got)[finite], bits(want)[finite])
+
+
 def test_matmul_tensor_cores_formula(lib, mm):
     """forward-check.mjs's matmul_q8r formula through the tensor-core path: its activations repeated to 24 tokens."""
     for groups in mm.GROUPS:

@@ -2,7 +2,7 @@
 """bench.py — decode+prefill tok/s of the int8 forward engine: the Llama-3-8B shape, 64 sequences of 512 prompt tokens
 + 256 greedy tokens, sharded by sequence across 1/2/4/8 GPUs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config c5|c4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config c5|c4|c3|c2]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
 One step is one batch of the workload through the engine's C ABI: `seqs` sequences in all (64) of `prompt` (512)
@@ -17,7 +17,8 @@ of the step (CUDA events around the engine's calls and the all-gather, max over 
 host-buffer calls, by the host clock around each step, host-to-device copies of the prompts and device-to-host reads
 of the generated ids inside. roofline: the dominant kernel (the int8 matmul) timed alone at the decode step's shapes
 with CUDA events, algorithmic bytes over its duration against the measured HBM copy bandwidth. c4_matmul: the matmul
-alone at the 8B projection shapes at M = 1, 8, 64, 512 tokens. cpu_baseline: the oracle (a C++ restatement of the
+alone at the 8B projection shapes at M = 1, 8, 64, 512 tokens; c3_decode_attention and c2_prefill_attention: the
+decode attention and the tensor-core prefill attention at their own configurations. cpu_baseline: the oracle (a C++ restatement of the
 reference's WASM-SIMD path, built for the host's own CPU, every host thread) on a bounded sample of the workload.
 
 --impl reference: the reference's CPU path on this host (the oracle port: the reference's AssemblyScript kernels

@@ -254,7 +254,10 @@ def reference_arm(args):
     return 0
 
 
-TRAFFIC_RATIO = 139.386 / 139.757  # measured DRAM bytes / algorithmic bytes of one decode-shape matmul launch
+# measured DRAM bytes / algorithmic bytes of the decode-shape matmul launches (ncu, one launch each): q8_gemm_tc at
+# 28672 x 4096 136.25 / 139.76 MB, q8_gemm_lanes at 4096 x 14336 67.91 / 68.14 MB; weighted by the bytes each kernel
+# moves in a decode pass (q|k|v, w1|w3 and the classifier on the first, o and w2 on the second: 5724 and 2720 MB)
+TRAFFIC_RATIO = (5724 * (136.25 / 139.76) + 2720 * (67.91 / 68.14)) / (5724 + 2720)
 
 
 def matmul_roofline(eng, M, peaks, reps=3):
@@ -266,13 +269,14 @@ def matmul_roofline(eng, M, peaks, reps=3):
     per_launch_bytes = nbytes / launches
     achieved = per_launch_bytes / per_launch_s / 1e9
     peak = float(peaks["hbm_gbs"])
-    return {"kernel": "q8_gemm_tc (int8 group-32 matmul, tcgen05, exact order)" if M >= 16 else
+    return {"kernel": "q8_gemm_tc + q8_gemm_lanes (int8 group-32 matmul, tcgen05, exact order)" if M >= 2 else
             "matvec_kernel (int8 group-32 matmul, exact order)", "bound": "hbm",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            # DRAM bytes per launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one launch of the
-            # 28672 x 4096 matrix at 64 tokens read and wrote 0.997 of its algorithmic bytes (every byte once);
-            # the same ratio over this pass's launches
-            "traffic": TRAFFIC_RATIO * per_launch_bytes, "traffic_source": "ncu, 28672x4096 at 64 tokens, scaled",
+            # DRAM bytes per launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one launch of each
+            # kernel at 64 tokens read and wrote 0.975 and 0.997 of its algorithmic bytes (every byte once); their
+            # byte-weighted ratio over this pass's launches
+            "traffic": TRAFFIC_RATIO * per_launch_bytes,
+            "traffic_source": "ncu, 28672x4096 (q8_gemm_tc) and 4096x14336 (q8_gemm_lanes) at 64 tokens, scaled",
             "M": M, "per_launch_us": per_launch_s * 1e6, "launches_per_pass": launches,
             "algorithmic_bytes_per_launch": per_launch_bytes, "pass_ms": ms}
 

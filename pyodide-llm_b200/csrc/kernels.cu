@@ -234,11 +234,21 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
   extern __shared__ float sq[];
   const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   const float *xr = x + (int64_t)tok * x_stride;
-  const float s = norm_scale(xr, n, eps, sq, part);
   const int ng = n >> 5;
-  for (int g = warp; g < ng; g += warps) {
+  // this warp's first NQ_PRE groups' values and weights, read before the norm's serial chain (they do not depend on
+  // it), so that the quantization after it waits on no memory
+  constexpr int NQ_PRE = 4;
+  float xv[NQ_PRE], wv[NQ_PRE];
+#pragma unroll
+  for (int u = 0; u < NQ_PRE; u++) {
+    const int g = warp + u * warps;
+    xv[u] = g < ng ? xr[g * 32 + lane] : 0.0f;
+    wv[u] = g < ng ? w[g * 32 + lane] : 0.0f;
+  }
+  const float s = norm_scale(xr, n, eps, sq, part);
+  auto group = [&](int g, float xj, float wj) {
     const int j = g * 32 + lane;
-    float v = fmul(w[j], fmul(s, xr[j]));
+    float v = fmul(wj, fmul(s, xj));
     if (out_f) out_f[(int64_t)tok * out_stride + j] = v;
     for (int c = 0; c < nch; c++) {
       if (channels[c] == j) {
@@ -248,7 +258,13 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
     }
     quantize_group(v, lane, bias, xq + (int64_t)tok * q_stride + g * 32,
                    xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
+  };
+#pragma unroll
+  for (int u = 0; u < NQ_PRE; u++) {
+    const int g = warp + u * warps;
+    if (g < ng) group(g, xv[u], wv[u]);
   }
+  for (int g = warp + NQ_PRE * warps; g < ng; g += warps) group(g, xr[g * 32 + lane], w[g * 32 + lane]);
 }
 
 __global__ void rmsnorm_kernel(float *out, const float *x, const float *w, int n, float eps, int64_t stride) {

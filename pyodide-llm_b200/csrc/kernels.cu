@@ -312,6 +312,52 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
                  xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
+// swiglu_quantize_kernel with four consecutive values a thread (16-byte loads): eight lanes a group, four groups a
+// warp. A thread's four values are one of each of quantize_x's lane classes (index mod 4), so each class's largest
+// |value| is a max over the group's eight lanes; then the same scalar comparisons, scale and rounding as
+// quantize_group. grid (groups / 32 rounded up, tokens), 256 threads; h1, h3 rows and xq rows 16-byte aligned.
+__global__ void swiglu_quantize_v4_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias,
+                                          int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
+                                          int shift) {
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int n4 = n & ~3;
+  const int g = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + (lane >> 3), tok = blockIdx.y;
+  const bool live = g < (n >> 5);
+  const int j = g * 32 + sub * 4;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  if (live) {
+    const float4 a = *reinterpret_cast<const float4 *>(h1 + (int64_t)tok * stride + j);
+    const float4 b = *reinterpret_cast<const float4 *>(h3 + (int64_t)tok * stride + j);
+    const float va[4] = {a.x, a.y, a.z, a.w}, vb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const float e = j + c < n4 ? vexp(-va[c]) : fexp(-va[c]);
+      o[c] = fmul(fdiv(va[c], fadd(1.0f, e)), vb[c]);
+    }
+  }
+  // groupMax's lane-class maxima (kernel.ts:129-156): class c over the group's eight lanes
+  float m[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    m[c] = fabsf(o[c]);
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 1));
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 2));
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 4));
+  }
+  if (!live) return;
+  float amax = m[0];
+  if (m[1] > amax) amax = m[1];
+  if (m[2] > amax) amax = m[2];
+  if (m[3] > amax) amax = m[3];
+  const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
+  const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int c = 0; c < 4; c++) packed |= (uint32_t)(uint8_t)(int8_t)(quantize_one(o[c], inv, bias) - shift) << (8 * c);
+  *reinterpret_cast<uint32_t *>(xq + (int64_t)tok * q_stride + j) = packed;
+  if (sub == 0) xs[(int64_t)tok * s_stride + (int64_t)g * g_stride] = scale;
+}
+
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
                              float *x, int64_t x_stride) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -573,6 +619,15 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "swiglu+quantize: n must be whole groups of 32");
   if (count > 65535) return fail(B200FWD_EINVAL, "swiglu+quantize: more than 65535 tokens");
+  const bool v4 = reinterpret_cast<uintptr_t>(h1) % 16 == 0 && reinterpret_cast<uintptr_t>(h3) % 16 == 0 &&
+                  stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 && q_stride % 4 == 0;
+  if (v4) {
+    swiglu_quantize_v4_kernel<<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(h1, h3, stride, n, bias, xq,
+                                                                                      q_stride, xs, s_stride,
+                                                                                      g_stride, shift);
+    B200_LAUNCHED("swiglu_quantize_v4_kernel");
+    return 0;
+  }
   swiglu_quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq,
                                                                                  q_stride, xs, s_stride, g_stride,
                                                                                  shift);

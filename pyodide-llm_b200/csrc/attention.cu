@@ -187,20 +187,43 @@ __global__ void attn_softmax_tiled(float *att, const int32_t *pos, int pos0, int
   float *row = att + ((int64_t)tok * nh + h) * P;
   // the largest from -FLT_MAX, a NaN kept (kernel.ts:423-445: the order does not matter)
   float mx = -FLT_MAX;
-  for (int t = threadIdx.x; t < count; t += blockDim.x) mx = wmax(mx, row[t]);
+  for (int t = threadIdx.x; t < count; t += blockDim.x) {
+    const float v = row[t];
+    e[t] = v;  // the row stays in shared memory for the exponentials
+    mx = wmax(mx, v);
+  }
   for (int o = 16; o > 0; o >>= 1) mx = wmax(mx, __shfl_xor_sync(FULL, mx, o));
   if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
   __syncthreads();
   mx = -FLT_MAX;
   for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = wmax(mx, wm[w]);
   for (int t = threadIdx.x; t < count; t += blockDim.x) {
-    const float d = fsub(row[t], mx);
+    const float d = fsub(e[t], mx);  // this thread's own entry of the row
     e[t] = t < count4 ? vexp(d) : fexp(d);
   }
   __syncthreads();
   if (threadIdx.x < 4) {
+    // the lane's chain, its next sixteen terms read while the sixteen before are added
     float acc = 0.0f;
-    for (int t = threadIdx.x; t < count4; t += 4) acc = fadd(acc, e[t]);
+    int t = threadIdx.x;
+    if (t + 60 < count4) {
+      float cur[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) cur[u] = e[t + 4 * u];
+      for (; t + 124 < count4; t += 64) {
+        float nxt[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) nxt[u] = e[t + 64 + 4 * u];
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) cur[u] = nxt[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+      t += 64;
+    }
+    for (; t < count4; t += 4) acc = fadd(acc, e[t]);
     part[threadIdx.x] = acc;
   }
   __syncthreads();

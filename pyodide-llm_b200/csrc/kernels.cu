@@ -312,13 +312,14 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
                  xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
-// swiglu_quantize_kernel with four consecutive values a thread (16-byte loads): eight lanes a group, four groups a
-// warp. A thread's four values are one of each of quantize_x's lane classes (index mod 4), so each class's largest
-// |value| is a max over the group's eight lanes; then the same scalar comparisons, scale and rounding as
-// quantize_group. grid (groups / 32 rounded up, tokens), 256 threads; h1, h3 rows and xq rows 16-byte aligned.
-__global__ void swiglu_quantize_v4_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias,
-                                          int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
-                                          int shift) {
+// quantize_kernel (SWIGLU false: x = h1) and swiglu_quantize_kernel (true) with four consecutive values a thread
+// (16-byte loads): eight lanes a group, four groups a warp. A thread's four values are one of each of quantize_x's
+// lane classes (index mod 4), so each class's largest |value| is a max over the group's eight lanes; then the same
+// scalar comparisons, scale and rounding as quantize_group. grid (groups / 32 rounded up, tokens), 256 threads;
+// the input rows 16-byte aligned, the xq rows 4-byte aligned.
+template <bool SWIGLU>
+__global__ void quantize_v4_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int8_t *xq,
+                                   int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
   const int lane = threadIdx.x & 31, sub = lane & 7;
   const int n4 = n & ~3;
   const int g = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + (lane >> 3), tok = blockIdx.y;
@@ -327,12 +328,19 @@ __global__ void swiglu_quantize_v4_kernel(const float *h1, const float *h3, int6
   float o[4] = {0.f, 0.f, 0.f, 0.f};
   if (live) {
     const float4 a = *reinterpret_cast<const float4 *>(h1 + (int64_t)tok * stride + j);
-    const float4 b = *reinterpret_cast<const float4 *>(h3 + (int64_t)tok * stride + j);
-    const float va[4] = {a.x, a.y, a.z, a.w}, vb[4] = {b.x, b.y, b.z, b.w};
+    const float va[4] = {a.x, a.y, a.z, a.w};
+    if (SWIGLU) {
+      // kernel.ts:654-667 swiglu (vexp on the fours, fexp after them)
+      const float4 b = *reinterpret_cast<const float4 *>(h3 + (int64_t)tok * stride + j);
+      const float vb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const float e = j + c < n4 ? vexp(-va[c]) : fexp(-va[c]);
-      o[c] = fmul(fdiv(va[c], fadd(1.0f, e)), vb[c]);
+      for (int c = 0; c < 4; c++) {
+        const float e = j + c < n4 ? vexp(-va[c]) : fexp(-va[c]);
+        o[c] = fmul(fdiv(va[c], fadd(1.0f, e)), vb[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; c++) o[c] = va[c];
     }
   }
   // groupMax's lane-class maxima (kernel.ts:129-156): class c over the group's eight lanes
@@ -607,6 +615,14 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
   if (count <= 0) return 0;
   if (n % 32) return fail(B200FWD_EINVAL, "quantize_x: n must be whole groups of 32");
   if (count > 65535) return fail(B200FWD_EINVAL, "quantize_x: more than 65535 tokens");
+  if (reinterpret_cast<uintptr_t>(x) % 16 == 0 && x_stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 &&
+      q_stride % 4 == 0) {
+    quantize_v4_kernel<false><<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(x, nullptr, x_stride, n, bias,
+                                                                                       xq, q_stride, xs, s_stride,
+                                                                                       g_stride, shift);
+    B200_LAUNCHED("quantize_v4_kernel");
+    return 0;
+  }
   quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride,
                                                                           xs, s_stride, g_stride, shift);
   B200_LAUNCHED("quantize_kernel");
@@ -622,10 +638,10 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
   const bool v4 = reinterpret_cast<uintptr_t>(h1) % 16 == 0 && reinterpret_cast<uintptr_t>(h3) % 16 == 0 &&
                   stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 && q_stride % 4 == 0;
   if (v4) {
-    swiglu_quantize_v4_kernel<<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(h1, h3, stride, n, bias, xq,
+    quantize_v4_kernel<true><<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(h1, h3, stride, n, bias, xq,
                                                                                       q_stride, xs, s_stride,
                                                                                       g_stride, shift);
-    B200_LAUNCHED("swiglu_quantize_v4_kernel");
+    B200_LAUNCHED("quantize_v4_kernel<swiglu>");
     return 0;
   }
   swiglu_quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq,

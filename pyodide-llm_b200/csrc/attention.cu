@@ -237,6 +237,65 @@ __global__ void attn_softmax_tiled(float *att, const int32_t *pos, int pos0, int
   for (int t = threadIdx.x; t < count; t += blockDim.x) row[t] = fmul(e[t], inv);
 }
 
+// attn_softmax_tiled for rows of at most SOFTMAX_ROW_MAX positions: one warp a (token, head) row, SOFTMAX_ROWS rows a
+// block, each warp's row in its own part of shared memory. The same steps in the same order: the largest (any order),
+// the exponentials (vexp on the fours, fexp after), four lane chains over the fours then hsum and the rest, times
+// 1/sum. grid (ceil(count * nh / SOFTMAX_ROWS)), 32 * SOFTMAX_ROWS threads.
+constexpr int SOFTMAX_ROWS = 8;
+constexpr int SOFTMAX_ROW_MAX = 1024;
+__global__ void __launch_bounds__(32 * SOFTMAX_ROWS)
+    attn_softmax_rows(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1, int count_tokens) {
+  __shared__ float rows[SOFTMAX_ROWS][SOFTMAX_ROW_MAX];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int r = blockIdx.x * SOFTMAX_ROWS + w;
+  if (r >= count_tokens * nh) return;
+  const int tok = r / nh, h = r % nh;
+  if (h < h0 || h >= h1) return;
+  const int count = pos_of(pos, pos0, tok) + 1, count4 = count & ~3;
+  float *row = att + ((int64_t)tok * nh + h) * P;
+  float *e = rows[w];
+  float mx = -FLT_MAX;
+  for (int t = lane; t < count; t += 32) {
+    const float v = row[t];
+    e[t] = v;
+    mx = wmax(mx, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = wmax(mx, __shfl_xor_sync(FULL, mx, o));
+  for (int t = lane; t < count; t += 32) {
+    const float d = fsub(e[t], mx);
+    e[t] = t < count4 ? vexp(d) : fexp(d);
+  }
+  __syncwarp();
+  float acc = 0.0f;
+  if (lane < 4) {
+    int t = lane;
+    if (t + 60 < count4) {
+      float cur[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) cur[u] = e[t + 4 * u];
+      for (; t + 124 < count4; t += 64) {
+        float nxt[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) nxt[u] = e[t + 64 + 4 * u];
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) cur[u] = nxt[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = fadd(acc, cur[u]);
+      t += 64;
+    }
+    for (; t < count4; t += 4) acc = fadd(acc, e[t]);
+  }
+  const float p0 = __shfl_sync(FULL, acc, 0), p1 = __shfl_sync(FULL, acc, 1);
+  const float p2 = __shfl_sync(FULL, acc, 2), p3 = __shfl_sync(FULL, acc, 3);
+  float sum = fadd(fadd(fadd(p0, p1), p2), p3);
+  for (int t = count4; t < count; t++) sum = fadd(sum, e[t]);
+  const float inv = fdiv(1.0f, sum);
+  for (int t = lane; t < count; t += 32) row[t] = fmul(e[t], inv);
+}
+
 // one output value's step over four positions (kernel.ts:535-545): below the head's fours the products in pairs,
 // past them one after another
 __device__ __forceinline__ float four(float o, float w0, float w1, float w2, float w3, float v0, float v1, float v2,
@@ -641,6 +700,21 @@ __global__ void __launch_bounds__(32)
   }
 }
 
+// the softmax of count tokens' rows: a warp a row where the longest fits SOFTMAX_ROW_MAX, else a block a row
+int launch_softmax(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1, int count, int max_count,
+                   size_t smem_soft, cudaStream_t stream) {
+  if (max_count <= SOFTMAX_ROW_MAX) {
+    const int64_t rows = (int64_t)count * nh;
+    attn_softmax_rows<<<(unsigned)((rows + SOFTMAX_ROWS - 1) / SOFTMAX_ROWS), 32 * SOFTMAX_ROWS, 0, stream>>>(
+        att, pos, pos0, P, nh, h0, h1, count);
+    B200_LAUNCHED("attn_softmax_rows");
+    return 0;
+  }
+  attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
+  B200_LAUNCHED("attn_softmax_tiled");
+  return 0;
+}
+
 template <bool HALF, int G>
 int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                  float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
@@ -658,8 +732,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
                                   stream>>>(q, q_stride, kc, att, seq, pos, pos0,
                                                                             seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
     B200_LAUNCHED("attn_scores_decode");
-    attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
-    B200_LAUNCHED("attn_softmax_tiled");
+    CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
     // the head's values split over `parts` blocks per token (more blocks streaming at once; the positions stay in
     // one chain per value): the most parts, up to two (measured best at 64 sequences of 512 to 8192 positions: 4 as
     // fast, 8 slower), whose rows are whole 16-byte pieces of an even number of values and that leave a block at
@@ -709,8 +782,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
   attn_scores_tiled<HALF, G><<<dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream>>>(
       q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
   B200_LAUNCHED("attn_scores_tiled");
-  attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
-  B200_LAUNCHED("attn_softmax_tiled");
+  CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
   attn_values_tiled<HALF, G><<<dim3(nkv, ntiles), threads, smem_values, stream>>>(
       out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);

@@ -126,7 +126,7 @@ template <bool HALF, int G>
 __global__ void __launch_bounds__(ATT_CH)
     attn_scores_tiled(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
                       const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
-                      int hs, int h0, int h1, int vec) {
+                      int hs, int h0, int h1, int vec, float one) {
   extern __shared__ float sm[];
   const int kvh = blockIdx.y, chunk = blockIdx.x;
   const Tile tl = tile_of(tiles, blockIdx.z);
@@ -139,38 +139,48 @@ __global__ void __launch_bounds__(ATT_CH)
   float *qs = sm + ATT_CH * pitch;       // [count][G][hsp]
   const int64_t sq = seq ? seq[tl.first] : 0;
   stage_rows<HALF>(kf, pitch, kc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs, kvDim, hs, rows, vec);
-  for (int idx = threadIdx.x; idx < tl.count * G * hs; idx += blockDim.x) {
-    const int i = idx / (G * hs), r = idx % (G * hs), gg = r / hs, d = r % hs;
-    qs[(i * G + gg) * hsp + d] = q[(int64_t)(tl.first + i) * q_stride + (int64_t)kvh * G * hs + r];
+  if (hsp == hs && (G * hs) % 4 == 0 && q_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+    // each token's G heads are one contiguous run of G * hs floats: 16-byte copies, no division
+    for (int i = 0; i < tl.count; i++) {
+      const float4 *src = reinterpret_cast<const float4 *>(q + (int64_t)(tl.first + i) * q_stride + (int64_t)kvh * G * hs);
+      float4 *dst = reinterpret_cast<float4 *>(qs + i * G * hs);
+      for (int r = threadIdx.x; r < G * hs / 4; r += blockDim.x) dst[r] = src[r];
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < tl.count * G * hs; idx += blockDim.x) {
+      const int i = idx / (G * hs), r = idx % (G * hs), gg = r / hs, d = r % hs;
+      qs[(i * G + gg) * hsp + d] = q[(int64_t)(tl.first + i) * q_stride + (int64_t)kvh * G * hs + r];
+    }
   }
   __syncthreads();
   const int t = threadIdx.x, p = c0 + t;
   if (t >= rows) return;
   const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
   const float *krow = kf + t * pitch;
+  const uint64_t one2 = pk(one, one);
   for (int i = 0; i < tl.count; i++) {
     const int tok = tl.first + i;
     if (p > pos_of(pos, pos0, tok)) continue;  // causal: a token reads the positions up to its own
-    float a[G][4];
+    // lane accumulators (0, 1) and (2, 3) of each head, paired (each lane rounded on its own): lane k takes the
+    // dims 4i + k
+    uint64_t a01[G], a23[G];
 #pragma unroll
-    for (int g = 0; g < G; g++) a[g][0] = a[g][1] = a[g][2] = a[g][3] = 0.0f;
+    for (int g = 0; g < G; g++) a01[g] = a23[g] = 0;
     const float *qi = qs + i * G * hsp;
     for (int j = 0; j < hs4; j += 4) {
-      const float4 k4 = *reinterpret_cast<const float4 *>(krow + j);
+      const ulonglong2 k4 = *reinterpret_cast<const ulonglong2 *>(krow + j);
 #pragma unroll
       for (int g = 0; g < G; g++) {
-        const float4 q4 = *reinterpret_cast<const float4 *>(qi + g * hsp + j);
-        a[g][0] = fadd(a[g][0], fmul(q4.x, k4.x));
-        a[g][1] = fadd(a[g][1], fmul(q4.y, k4.y));
-        a[g][2] = fadd(a[g][2], fmul(q4.z, k4.z));
-        a[g][3] = fadd(a[g][3], fmul(q4.w, k4.w));
+        const ulonglong2 q4 = *reinterpret_cast<const ulonglong2 *>(qi + g * hsp + j);
+        a01[g] = fma2(one2, a01[g], mul2(q4.x, k4.x));
+        a23[g] = fma2(one2, a23[g], mul2(q4.y, k4.y));
       }
     }
 #pragma unroll
     for (int g = 0; g < G; g++) {
       const int h = kvh * G + g;
       if (h < h0 || h >= h1) continue;
-      float s = fadd(fadd(a[g][0], a[g][2]), fadd(a[g][1], a[g][3]));
+      float s = fadd(fadd(lo(a01[g]), lo(a23[g])), fadd(hi(a01[g]), hi(a23[g])));  // (l0+l2)+(l1+l3)
       for (int j = hs4; j < hs; j++) s = fadd(s, fmul(qi[g * hsp + j], krow[j]));
       att[((int64_t)tok * nh + h) * P + p] = fmul(s, isq);
     }
@@ -780,7 +790,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
   B200_CUDA(cudaFuncSetAttribute(attn_values_tiled<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)MAX_TILE_SMEM));
   attn_scores_tiled<HALF, G><<<dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream>>>(
-      q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
+      q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_scores_tiled");
   CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;

@@ -317,7 +317,8 @@ __device__ __forceinline__ float four(float o, float w0, float w1, float w2, flo
 template <bool HALF, int G>
 __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc, const float *att,
                                   const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles,
-                                  int64_t seq_stride, int P, int nh, int nkv, int hs, int h0, int h1, int vec) {
+                                  int64_t seq_stride, int P, int nh, int nkv, int hs, int h0, int h1, int vec,
+                                  float one) {
   extern __shared__ float sm[];
   const int kvh = blockIdx.x;
   const Tile tl = tile_of(tiles, blockIdx.y);
@@ -331,9 +332,12 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
   const bool has1 = j1 < hs;
   const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
   const int64_t sq = seq ? seq[tl.first] : 0;
-  float o0[ATT_TT], o1[ATT_TT];
+  // the two values' sums of each token, paired (value j0 low, j1 high; each rounded on its own)
+  uint64_t o[ATT_TT];
 #pragma unroll
-  for (int i = 0; i < ATT_TT; i++) o0[i] = o1[i] = 0.0f;
+  for (int i = 0; i < ATT_TT; i++) o[i] = 0;
+  const uint64_t one2 = pk(one, one);
+  const bool pair4 = has1 && j1 < hs4;  // both values in the head's fours: the paired step
   for (int c0 = 0; c0 <= last; c0 += ATT_CH) {
     const int rows = min(ATT_CH, last + 1 - c0);
     __syncthreads();  // the previous chunk is done with
@@ -364,14 +368,24 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
         const float *w = wsm + (i * G + g) * ATT_CH + p;
         if (P0 + 4 <= count4) {
           const float4 w4 = *reinterpret_cast<const float4 *>(w);
-          o0[i] = four(o0[i], w4.x, w4.y, w4.z, w4.w, v0[0], v0[1], v0[2], v0[3], j0 < hs4);
-          if (has1) o1[i] = four(o1[i], w4.x, w4.y, w4.z, w4.w, v1[0], v1[1], v1[2], v1[3], j1 < hs4);
+          if (pair4) {
+            // ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) for both values at once, then added to the sums
+            const uint64_t s01 = fma2(one2, mul2(pk(w4.x, w4.x), pk(v0[0], v1[0])), mul2(pk(w4.y, w4.y), pk(v0[1], v1[1])));
+            const uint64_t s23 = fma2(one2, mul2(pk(w4.z, w4.z), pk(v0[2], v1[2])), mul2(pk(w4.w, w4.w), pk(v0[3], v1[3])));
+            o[i] = fma2(one2, o[i], fma2(one2, s01, s23));
+          } else {
+            const float a0 = four(lo(o[i]), w4.x, w4.y, w4.z, w4.w, v0[0], v0[1], v0[2], v0[3], j0 < hs4);
+            const float a1 = has1 ? four(hi(o[i]), w4.x, w4.y, w4.z, w4.w, v1[0], v1[1], v1[2], v1[3], j1 < hs4) : 0.0f;
+            o[i] = pk(a0, a1);
+          }
         } else if (P0 < count) {
           // the positions past the fours, one at a time (kernel.ts:548-564)
+          float a0 = lo(o[i]), a1 = hi(o[i]);
           for (int u = 0; u < 4 && P0 + u < count; u++) {
-            o0[i] = fadd(o0[i], fmul(w[u], v0[u]));
-            if (has1) o1[i] = fadd(o1[i], fmul(w[u], v1[u]));
+            a0 = fadd(a0, fmul(w[u], v0[u]));
+            if (has1) a1 = fadd(a1, fmul(w[u], v1[u]));
           }
+          o[i] = pk(a0, a1);
         }
       }
     }
@@ -380,9 +394,9 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
 #pragma unroll
   for (int i = 0; i < ATT_TT; i++) {
     if (i >= tl.count) break;
-    float *o = out + (int64_t)(tl.first + i) * out_stride + h * hs;
-    o[j0] = o0[i];
-    if (has1) o[j1] = o1[i];
+    float *dst = out + (int64_t)(tl.first + i) * out_stride + h * hs;
+    dst[j0] = lo(o[i]);
+    if (has1) dst[j1] = hi(o[i]);
   }
 }
 
@@ -795,7 +809,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
   CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
   attn_values_tiled<HALF, G><<<dim3(nkv, ntiles), threads, smem_values, stream>>>(
-      out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec);
+      out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_values_tiled");
   return 0;
 }

@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(ATT_CH)
     attn_scores_tiled(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
                       const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
                       int hs, int h0, int h1, int vec, float one) {
+  pdl_begin();
   extern __shared__ float sm[];
   const int kvh = blockIdx.y, chunk = blockIdx.x;
   const Tile tl = tile_of(tiles, blockIdx.z);
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(ATT_CH)
 }
 
 __global__ void attn_softmax_tiled(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1) {
+  pdl_begin();
   extern __shared__ float e[];
   __shared__ float part[5];
   __shared__ float wm[32];
@@ -255,6 +257,7 @@ constexpr int SOFTMAX_ROWS = 8;
 constexpr int SOFTMAX_ROW_MAX = 1024;
 __global__ void __launch_bounds__(32 * SOFTMAX_ROWS)
     attn_softmax_rows(float *att, const int32_t *pos, int pos0, int P, int nh, int h0, int h1, int count_tokens) {
+  pdl_begin();
   __shared__ float rows[SOFTMAX_ROWS][SOFTMAX_ROW_MAX];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int r = blockIdx.x * SOFTMAX_ROWS + w;
@@ -319,6 +322,7 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
                                   const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles,
                                   int64_t seq_stride, int P, int nh, int nkv, int hs, int h0, int h1, int vec,
                                   float one) {
+  pdl_begin();
   extern __shared__ float sm[];
   const int kvh = blockIdx.x;
   const Tile tl = tile_of(tiles, blockIdx.y);
@@ -413,6 +417,7 @@ __global__ void __launch_bounds__(DEC_POS)
     attn_scores_decode(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
                        const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
                        int h1, float one) {
+  pdl_begin();
   extern __shared__ __align__(16) float qs[];  // [G][hs], then the chunk's keys: DEC_POS rows of hs * ES + 16 bytes
   constexpr int PER = HALF ? 8 : 4, ES = HALF ? 2 : 4;
   const int kvh = blockIdx.y, tok = blockIdx.z;
@@ -502,6 +507,7 @@ __global__ void __launch_bounds__(1024)
     attn_values_decode(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
                        const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
                        int h1, int wvec, float one) {
+  pdl_begin();
   extern __shared__ __align__(16) uint8_t vsm[];
   constexpr int ES = HALF ? 2 : 4;
   const int kvh = blockIdx.x, tok = blockIdx.y;
@@ -632,6 +638,7 @@ __global__ void __launch_bounds__(32)
     attn_values_decode_h(float *out, int64_t out_stride, const uint16_t *vc, const float *att, const int32_t *seq,
                          const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
                          int h1, float one) {
+  pdl_begin();
   __shared__ __align__(16) uint32_t vbuf[HNB][HCH][32];  // raw float16 pairs: [chunk][position][lane]
   __shared__ __align__(16) uint64_t wbuf[2][G][HCH];     // the weights x 2^112, twice: [chunk & 1][head][position]
   const int parts = hs >> 6;
@@ -729,12 +736,12 @@ int launch_softmax(float *att, const int32_t *pos, int pos0, int P, int nh, int 
                    size_t smem_soft, cudaStream_t stream) {
   if (max_count <= SOFTMAX_ROW_MAX) {
     const int64_t rows = (int64_t)count * nh;
-    attn_softmax_rows<<<(unsigned)((rows + SOFTMAX_ROWS - 1) / SOFTMAX_ROWS), 32 * SOFTMAX_ROWS, 0, stream>>>(
+    launch(attn_softmax_rows, (unsigned)((rows + SOFTMAX_ROWS - 1) / SOFTMAX_ROWS), 32 * SOFTMAX_ROWS, 0, stream,
         att, pos, pos0, P, nh, h0, h1, count);
     B200_LAUNCHED("attn_softmax_rows");
     return 0;
   }
-  attn_softmax_tiled<<<dim3(nh, count), 256, smem_soft, stream>>>(att, pos, pos0, P, nh, h0, h1);
+  launch(attn_softmax_tiled, dim3(nh, count), 256, smem_soft, stream, att, pos, pos0, P, nh, h0, h1);
   B200_LAUNCHED("attn_softmax_tiled");
   return 0;
 }
@@ -752,8 +759,8 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     if (smem_scores > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a key chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_scores_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));
-    attn_scores_decode<HALF, G><<<dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS, smem_scores,
-                                  stream>>>(q, q_stride, kc, att, seq, pos, pos0,
+    launch(attn_scores_decode<HALF, G>, dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS, smem_scores,
+                                  stream, q, q_stride, kc, att, seq, pos, pos0,
                                                                             seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
     B200_LAUNCHED("attn_scores_decode");
     CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
@@ -767,7 +774,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
       return c == 1 || c == 2 || c == 4 || c == 8 ? c : 2;
     }();
     if (HALF && hs % 64 == 0) {
-      attn_values_decode_h<G><<<dim3(nkv * (hs / 64), count), 32, 0, stream>>>(
+      launch(attn_values_decode_h<G>, dim3(nkv * (hs / 64), count), 32, 0, stream,
           out, out_stride, static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
           1.0f);
       B200_LAUNCHED("attn_values_decode_h");
@@ -786,7 +793,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));
-    attn_values_decode<HALF, G><<<dim3(nkv, count, parts), threads, smem_values, stream>>>(
+    launch(attn_values_decode<HALF, G>, dim3(nkv, count, parts), threads, smem_values, stream,
         out, out_stride, vc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
         P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0, 1.0f);
     B200_LAUNCHED("attn_values_decode");
@@ -803,12 +810,12 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
                                  (int)MAX_TILE_SMEM));
   B200_CUDA(cudaFuncSetAttribute(attn_values_tiled<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)MAX_TILE_SMEM));
-  attn_scores_tiled<HALF, G><<<dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream>>>(
+  launch(attn_scores_tiled<HALF, G>, dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream,
       q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_scores_tiled");
   CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
-  attn_values_tiled<HALF, G><<<dim3(nkv, ntiles), threads, smem_values, stream>>>(
+  launch(attn_values_tiled<HALF, G>, dim3(nkv, ntiles), threads, smem_values, stream,
       out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_values_tiled");
   return 0;

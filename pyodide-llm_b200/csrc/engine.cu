@@ -11,6 +11,7 @@
 // run() is forward.js run() (forward.js:452-531) over tokens that may belong to different slots.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <initializer_list>
 #include <cstring>
 #include <mutex>
@@ -38,6 +39,14 @@ int fail(int code, const std::string &message) {
 int cuda_fail(cudaError_t e, const char *what) {
   return fail(e == cudaErrorMemoryAllocation ? B200FWD_ENOMEM : B200FWD_ECUDA,
               std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+bool pdl_on() {
+  static const bool on = [] {
+    const char *v = std::getenv("B200FWD_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 namespace {

@@ -91,6 +91,7 @@ __global__ void __cluster_dims__(LANES, 1, 1) __launch_bounds__(THREADS, 1)
                   float one) {
   using T = LTile<BN>;
   constexpr int STAGES = T::STAGES, SLOTS = T::SLOTS, TPW = T::TPW;
+  pdl_launch_dependents();
   extern __shared__ uint8_t raw[];
   LSmem<BN> &s = *reinterpret_cast<LSmem<BN> *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,6 +131,8 @@ __global__ void __cluster_dims__(LANES, 1, 1) __launch_bounds__(THREADS, 1)
   __syncthreads();
   fence_after();
   cluster_sync();  // every CTA's barriers are initialized before any arrives on them from another CTA
+  // the set-up above touches no global memory; the kernel before this one has completed from here on
+  pdl_wait();
   const uint32_t tmem = s.tmem_base;
 
   if (warp < EPI_WARP0) {
@@ -424,7 +427,7 @@ int launch_gemm_lanes(const GemmMaps &maps, const GemmArgs &args, int bn, cudaSt
   const int64_t tiles = (int64_t)((args.rows + BM - 1) / BM) * ((args.count + bn - 1) / bn);
   const dim3 grid((unsigned)(LANES * std::min<int64_t>(tiles, fit)));
 #define B200_LANES_LAUNCH(W) \
-  q8_gemm_lanes<W><<<grid, THREADS, lanes_smem_bytes<W>(), stream>>>(maps.w, maps.x, maps.ws, maps.xs, args, 1.0f)
+  launch(q8_gemm_lanes<W>, grid, THREADS, lanes_smem_bytes<W>(), stream, maps.w, maps.x, maps.ws, maps.xs, args, 1.0f)
   if (bn == 16)
     B200_LANES_LAUNCH(16);
   else if (bn == 32)

@@ -192,18 +192,9 @@ struct Smem {
   uint32_t tmem_base;
 };
 
-// TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes
+// TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes (tiles of 16 and 32 tokens)
 template <int TPW>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[TPW]);
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-      "[%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
 template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
@@ -217,17 +208,163 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
+// 16 TMEM lanes x 16 columns (two 256-bit repetitions) from lane taddr.lane: thread t holds lane t/4 in r[0], r[1]
+// (columns 2(t%4), +1) and r[4], r[5] (columns 8 + 2(t%4), +1), and lane t/4 + 8 in r[2], r[3] and r[6], r[7] (the same
+// columns)
+__device__ __forceinline__ void tmem_ld_16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) { return (uint64_t)lo | ((uint64_t)hi << 32); }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// one * a + b rounded once, one = 1.0f handed over at run time: a + b, and no product can be folded into the add
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// The epilogue of 64-token tiles. Epilogue warp w reads TMEM lane quarter w % 4 and token columns (w - 4) / 4 * 16 ..
+// + 16 as 16x256b fragments of both 16-lane halves, so that thread t keeps four rows (quarter * 32 + t/4 + 8i) x two
+// token pairs (8p + 2(t%4), +1 of the warp's sixteen). Each activation-scale pair a thread reads from shared memory
+// then serves four rows (against one with a thread a row), and the two tokens of a pair, adjacent in the fragment, go
+// through each float operation together (.f32x2: each half rounded on its own, as the scalar operation rounds it):
+// half the shared-memory reads of scales and half the float instructions. The arithmetic per (row, token, group) and
+// its order are those of the general epilogue below.
+template <bool TAIL>
+__device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int quarter, int sub, int lane,
+                                             const GemmArgs &args, int tiles, int ntok, int kstages, int ng, int ng4,
+                                             float one) {
+  constexpr int BN = 64, STAGES = Tile<BN>::STAGES, SLOTS = Tile<BN>::SLOTS;
+  const int c = lane & 3, rq = lane >> 2;
+  const uint32_t t_lo = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 16), t_hi = t_lo + (16u << 16);
+  const uint64_t one2 = pk2(__float_as_uint(one), __float_as_uint(one));
+  Ring<STAGES> ring;
+  Ring<SLOTS> slots;
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+    uint64_t acc[4][2][4];  // [row rq + 8i][token pair p][chain lane j]
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int p = 0; p < 2; p++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][p][j] = 0;
+    for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+      const int st = ring.i, slot = slots.i;
+      mbar_wait(&s.full[st], ring.phase, args.error, 4);
+      const int groups = TAIL ? min(4, ng - 4 * k) : 4;
+      mbar_wait(&s.slot_full[slot], slots.phase, args.error, 5);
+      tc_fence_after();
+      const float *wq = &s.ws[st][quarter * 32 + rq][0];  // row rq + 8i's group j: wq[32 * i + j]
+      const float *xq = s.xs[st] + sub * 16 + 2 * c;      // group j's token pair p: xq[j * BN + 8 * p], two floats
+      const bool whole = !TAIL || 4 * k + 4 <= ng4;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        uint32_t v[2][8];  // the two 16-lane halves' fragments
+        uint32_t wv[4];
+        uint64_t x2[2];
+        if (j < groups) {
+          const uint32_t col = (uint32_t)((slot * 4 + j) * BN);
+          tmem_ld_16x256_x2(t_lo + col, v[0]);
+          tmem_ld_16x256_x2(t_hi + col, v[1]);
+#pragma unroll
+          for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+#pragma unroll
+          for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
+          tmem_wait_ld();
+        }
+        // row rq + 8i, pair p: fragment registers 4p + 2(i & 1), +1 of half i >> 1
+        if (whole) {
+          // lane j of the chain takes group 4k + j: float(S) x (weight scale x activation scale), rounded once each
+          // (kernel_relaxed.ts:45,55), added into the lane
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+              const int r = 4 * p + 2 * (i & 1);
+              const uint64_t sums = pk2(v[i >> 1][r], v[i >> 1][r + 1]);
+              acc[i][p][j] = fma2(one2, acc[i][p][j], mul2(sums, mul2(pk2(wv[i], wv[i]), x2[p])));
+            }
+        } else {
+          // the stage of the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first (kept in
+          // lane 0), then each group in turn
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+              float x[2];
+#pragma unroll
+              for (int e = 0; e < 2; e++) {
+                auto part = [&](int l) { return e ? hi_f(acc[i][p][l]) : lo_f(acc[i][p][l]); };
+                x[e] = j == 0 ? __fadd_rn(__fadd_rn(__fadd_rn(part(0), part(1)), part(2)), part(3)) : part(0);
+                if (j < groups) {
+                  const float sum = __uint_as_float(v[i >> 1][4 * p + 2 * (i & 1) + e]);
+                  const float xs = e ? hi_f(x2[p]) : lo_f(x2[p]);
+                  x[e] = __fadd_rn(x[e], __fmul_rn(sum, __fmul_rn(__uint_as_float(wv[i]), xs)));
+                }
+              }
+              acc[i][p][0] = pk2(__float_as_uint(x[0]), __float_as_uint(x[1]));
+            }
+        }
+      }
+      // the slot goes back to the MMAs, the stage's shared memory to the producer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s.slot_empty[slot]);
+        mbar_arrive(&s.empty[st]);
+      }
+    }
+    if (!TAIL) {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int p = 0; p < 2; p++)
+          acc[i][p][0] = fma2(one2, fma2(one2, fma2(one2, acc[i][p][0], acc[i][p][1]), acc[i][p][2]), acc[i][p][3]);
+    }
+    // each store writes eight consecutive rows of four tokens (four 32-byte pieces)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int r = row0 + quarter * 32 + rq + 8 * i;
+      if (r >= args.rows) continue;
+#pragma unroll
+      for (int p = 0; p < 2; p++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const int tok = tok0 + sub * 16 + 8 * p + 2 * c + e;
+          if (tok < args.count) {
+            const float sum = e ? hi_f(acc[i][p][0]) : lo_f(acc[i][p][0]);
+            float *o = args.out + (int64_t)tok * args.out_stride + r;
+            *o = args.accumulate ? __fadd_rn(*o, sum) : sum;
+          }
+        }
+    }
+  }
+}
+
 // Warp roles: 0 TMA producer, 1 MMA issue, 2 and 3 idle, 4..19 epilogue. Epilogue warp w reads TMEM lane quarter
-// w % 4 (its 32 rows) and token columns (w - 4) / 4 * TPW .. + TPW, and keeps the reference's four chain accumulators of each of
-// its (row, token) in registers: the chains, their sum and the groups past the fours all happen in one thread. Tiles go round the blocks (tile = block, block + grid, ...): consecutive tiles share
-// their weight rows, so blocks that run together read each weight row once from HBM.
+// w % 4 (its 32 rows) and token columns (w - 4) / 4 * TPW .. + TPW (64-token tiles: epilogue_4x4 above), and keeps the
+// reference's four chain accumulators of each of its (row, token) in registers: the chains, their sum and the groups
+// past the fours all happen in one thread. Tiles go round the blocks (tile = block, block + grid, ...): consecutive
+// tiles share their weight rows, so blocks that run together read each weight row once from HBM.
 // TAIL: n / 32 is not a multiple of four (groups past the fours); without it every stage is four whole groups
 template <int BN, bool TAIL>
 __global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-               const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap, GemmArgs args) {
+               const __grid_constant__ CUtensorMap wsmap, const __grid_constant__ CUtensorMap xsmap, GemmArgs args,
+               float one) {
   using T = Tile<BN>;
   constexpr int STAGES = T::STAGES, SLOTS = T::SLOTS, TPW = T::TPW, GB = T::GB;
+  pdl_launch_dependents();
   extern __shared__ uint8_t raw[];
   Smem<BN> &s = *reinterpret_cast<Smem<BN> *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,6 +401,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // the set-up above touches no global memory; the kernel before this one (the activations' producer, or the
+  // residual's writer) has completed from here on
+  pdl_wait();
   const uint32_t tmem = s.tmem_base;
 
   if (warp < EPI_WARP0) {
@@ -332,89 +472,93 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
     // ---- epilogue
     const int quarter = warp % 4, sub = (warp - EPI_WARP0) / 4;
-    const int rl = quarter * 32 + lane;  // the row within the tile
-    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
-    Ring<STAGES> ring;
-    Ring<SLOTS> slots;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-      const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
-      float acc[TPW][4];  // chain lane j of token t
+    if constexpr (BN == 64) {
+      epilogue_4x4<TAIL>(s, tmem, quarter, sub, lane, args, tiles, ntok, kstages, ng, ng4, one);
+    } else {
+      const int rl = quarter * 32 + lane;  // the row within the tile
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
+      Ring<STAGES> ring;
+      Ring<SLOTS> slots;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+        float acc[TPW][4];  // chain lane j of token t
 #pragma unroll
-      for (int t = 0; t < TPW; t++)
+        for (int t = 0; t < TPW; t++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[t][j] = 0.f;
-      for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
-        const int st = ring.i, slot = slots.i;
-        mbar_wait(&s.full[st], ring.phase, args.error, 4);
-        const int groups = TAIL ? min(4, ng - 4 * k) : 4;
-        mbar_wait(&s.slot_full[slot], slots.phase, args.error, 5);
-        tc_fence_after();
-        const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
-        const bool whole = !TAIL || 4 * k + 4 <= ng4;
+          for (int j = 0; j < 4; j++) acc[t][j] = 0.f;
+        for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+          const int st = ring.i, slot = slots.i;
+          mbar_wait(&s.full[st], ring.phase, args.error, 4);
+          const int groups = TAIL ? min(4, ng - 4 * k) : 4;
+          mbar_wait(&s.slot_full[slot], slots.phase, args.error, 5);
+          tc_fence_after();
+          const float4 w4 = *reinterpret_cast<const float4 *>(s.ws[st][rl]);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          const float *xrow = s.xs[st] + sub * TPW;  // group j's scale of this warp's token t: xrow[j * BN + t]
+          const bool whole = !TAIL || 4 * k + 4 <= ng4;
 #pragma unroll
-        for (int j0 = 0; j0 < 4; j0 += GB) {
-          uint32_t v[GB][TPW];
+          for (int j0 = 0; j0 < 4; j0 += GB) {
+            uint32_t v[GB][TPW];
 #pragma unroll
-          for (int jj = 0; jj < GB; jj++)
-            if (j0 + jj < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j0 + jj) * BN), v[jj]);
-          tmem_wait_ld();
-          if (whole) {
-            // lane j of the chain takes group 4k + j: float(S) x (weight scale x activation scale), rounded once
-            // each (kernel_relaxed.ts:45,55), added into the lane
-#pragma unroll
-            for (int jj = 0; jj < GB; jj++) {
-              const int j = j0 + jj;
-#pragma unroll
-              for (int q = 0; q < TPW / 4; q++) {
-                const float4 x4 = *reinterpret_cast<const float4 *>(xrow + j * BN + 4 * q);
-                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-                for (int h = 0; h < 4; h++) {
-                  const int t = 4 * q + h;
-                  acc[t][j] = __fadd_rn(acc[t][j], __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xv[h])));
-                }
-              }
-            }
-          } else {
-            // the stage of the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
-            // (kept in acc[t][0]), then each group in turn
-#pragma unroll
-            for (int t = 0; t < TPW; t++) {
-              float x = j0 == 0 ? __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3])
-                                : acc[t][0];
+            for (int jj = 0; jj < GB; jj++)
+              if (j0 + jj < groups) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + j0 + jj) * BN), v[jj]);
+            tmem_wait_ld();
+            if (whole) {
+              // lane j of the chain takes group 4k + j: float(S) x (weight scale x activation scale), rounded once
+              // each (kernel_relaxed.ts:45,55), added into the lane
 #pragma unroll
               for (int jj = 0; jj < GB; jj++) {
                 const int j = j0 + jj;
-                if (j < groups)
-                  x = __fadd_rn(x, __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xrow[j * BN + t])));
+#pragma unroll
+                for (int q = 0; q < TPW / 4; q++) {
+                  const float4 x4 = *reinterpret_cast<const float4 *>(xrow + j * BN + 4 * q);
+                  const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                  for (int h = 0; h < 4; h++) {
+                    const int t = 4 * q + h;
+                    acc[t][j] = __fadd_rn(acc[t][j], __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xv[h])));
+                  }
+                }
               }
-              acc[t][0] = x;
+            } else {
+              // the stage of the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first
+              // (kept in acc[t][0]), then each group in turn
+#pragma unroll
+              for (int t = 0; t < TPW; t++) {
+                float x = j0 == 0 ? __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3])
+                                  : acc[t][0];
+#pragma unroll
+                for (int jj = 0; jj < GB; jj++) {
+                  const int j = j0 + jj;
+                  if (j < groups)
+                    x = __fadd_rn(x, __fmul_rn(__uint_as_float(v[jj][t]), __fmul_rn(wv[j], xrow[j * BN + t])));
+                }
+                acc[t][0] = x;
+              }
             }
           }
+          // the slot goes back to the MMAs, the stage's shared memory to the producer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&s.slot_empty[slot]);
+            mbar_arrive(&s.empty[st]);
+          }
         }
-        // the slot goes back to the MMAs, the stage's shared memory to the producer
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s.slot_empty[slot]);
-          mbar_arrive(&s.empty[st]);
+        if (!TAIL) {
+#pragma unroll
+          for (int t = 0; t < TPW; t++)
+            acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
         }
-      }
-      if (!TAIL) {
+        const int r = row0 + rl;
+        if (r < args.rows) {
 #pragma unroll
-        for (int t = 0; t < TPW; t++)
-          acc[t][0] = __fadd_rn(__fadd_rn(__fadd_rn(acc[t][0], acc[t][1]), acc[t][2]), acc[t][3]);
-      }
-      const int r = row0 + rl;
-      if (r < args.rows) {
-#pragma unroll
-        for (int t = 0; t < TPW; t++) {
-          const int tok = tok0 + sub * TPW + t;
-          if (tok < args.count) {
-            float *o = args.out + (int64_t)tok * args.out_stride + r;
-            *o = args.accumulate ? __fadd_rn(*o, acc[t][0]) : acc[t][0];
+          for (int t = 0; t < TPW; t++) {
+            const int tok = tok0 + sub * TPW + t;
+            if (tok < args.count) {
+              float *o = args.out + (int64_t)tok * args.out_stride + r;
+              *o = args.accumulate ? __fadd_rn(*o, acc[t][0]) : acc[t][0];
+            }
           }
         }
       }
@@ -539,7 +683,7 @@ int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &given, int bn, cudaStre
   const dim3 grid((unsigned)std::min<int64_t>(tiles, sms));
   const bool tail = (args.n / 32) % 4 != 0;
 #define B200_GEMM_LAUNCH(W, T) \
-  q8_gemm_tc<W, T><<<grid, THREADS, smem_bytes<W>(), stream>>>(maps.w, maps.x, maps.ws, maps.xs, args)
+  launch(q8_gemm_tc<W, T>, grid, THREADS, smem_bytes<W>(), stream, maps.w, maps.x, maps.ws, maps.xs, args, 1.0f)
   if (bn == 16)
     tail ? B200_GEMM_LAUNCH(16, true) : B200_GEMM_LAUNCH(16, false);
   else if (bn == 32)

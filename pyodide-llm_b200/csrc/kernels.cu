@@ -64,6 +64,7 @@ template <int MT, bool RELAXED>
 __global__ void __launch_bounds__(MV_WARPS * 32)
     matvec_kernel(MatJobs jobs, const int8_t *__restrict__ xq, const float *__restrict__ xs, int64_t q_stride,
                   int64_t s_stride, int64_t g_stride, int count) {
+  pdl_begin();
   constexpr int LANES = RELAXED ? 1 : 4;
   __shared__ float buf[MV_WARPS][MT][LANES][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -230,6 +231,7 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
                                      int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
                                      const int32_t *channels, int nch, float *picked, float *out_f,
                                      int64_t out_stride, int shift) {
+  pdl_begin();
   __shared__ float part[5];
   extern __shared__ float sq[];
   const int tok = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
@@ -268,6 +270,7 @@ __global__ void norm_quantize_kernel(const float *x, int64_t x_stride, const flo
 }
 
 __global__ void rmsnorm_kernel(float *out, const float *x, const float *w, int n, float eps, int64_t stride) {
+  pdl_begin();
   __shared__ float part[5];
   extern __shared__ float sq[];
   const float *xr = x + (int64_t)blockIdx.x * stride;
@@ -276,6 +279,7 @@ __global__ void rmsnorm_kernel(float *out, const float *x, const float *w, int n
 }
 
 __global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh, int hs, int rot) {
+  pdl_begin();
   const int turned = rot > 0 && rot < hs ? rot : hs;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int h = idx / (turned / 2), i = 2 * (idx % (turned / 2));
@@ -289,6 +293,7 @@ __global__ void rope_kernel(float *v, const float *fcr, const float *fci, int nh
 // grid (groups / 8 rounded up, tokens): a warp a group of 32
 __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bias, int count, int8_t *xq,
                                 int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), tok = blockIdx.y;
   if (g >= (n >> 5)) return;
@@ -300,6 +305,7 @@ __global__ void quantize_kernel(const float *x, int64_t x_stride, int n, int bia
 // kernel.ts:654-667 swiglu (vexp on the fours, fexp after them) feeding quantize_x; grid as quantize_kernel's
 __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int count,
                                        int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int n4 = n & ~3;
   const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), tok = blockIdx.y;
@@ -320,6 +326,7 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
 template <bool SWIGLU>
 __global__ void quantize_v4_kernel(const float *h1, const float *h3, int64_t stride, int n, int bias, int8_t *xq,
                                    int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride, int shift) {
+  pdl_begin();
   const int lane = threadIdx.x & 31, sub = lane & 7;
   const int n4 = n & ~3;
   const int g = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + (lane >> 3), tok = blockIdx.y;
@@ -368,6 +375,7 @@ __global__ void quantize_v4_kernel(const float *h1, const float *h3, int64_t str
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
                              float *x, int64_t x_stride) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)count * dim) return;
   const int t = (int)(i / dim), j = (int)(i % dim);
@@ -379,6 +387,7 @@ __global__ void rope_cache_kernel(float *q, int64_t q_stride, const float *k, co
                                   const float *cos, const float *sin, const int32_t *pos, const int32_t *seq,
                                   uint8_t *kc, uint8_t *vc, int64_t seq_stride, int half, int nh, int nkv, int hs,
                                   int rot) {
+  pdl_begin();
   const int tok = blockIdx.y;
   const int p = pos[tok];
   const int64_t sq = seq[tok];
@@ -436,6 +445,7 @@ __global__ void rope_cache_kernel(float *q, int64_t q_stride, const float *k, co
 
 __global__ void add_columns_kernel(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride,
                                    int nc, int n, int count) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)n * count) return;
   const int tok = (int)(i / n), j = (int)(i % n);
@@ -460,6 +470,7 @@ __device__ __forceinline__ bool better(float a, int ia, float b, int ib, int mod
 }
 
 __global__ void argmax_kernel(int32_t *out, const float *x, int64_t stride, int n, int mode) {
+  pdl_begin();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int tok = blockIdx.x;
@@ -489,6 +500,7 @@ __global__ void argmax_kernel(int32_t *out, const float *x, int64_t stride, int 
 
 __global__ void gather_rows_kernel(float *dst, int64_t dst_stride, const float *src, int64_t src_stride,
                                    const int32_t *idx, int count, int dim) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)count * dim) return;
   const int t = (int)(i / dim), j = (int)(i % dim);
@@ -498,6 +510,7 @@ __global__ void gather_rows_kernel(float *dst, int64_t dst_stride, const float *
 // scales of count tokens, one row per token (s_stride apart), into one row per group (t_stride apart)
 __global__ void scales_by_group_kernel(float *dst, int64_t t_stride, const float *src, int64_t s_stride, int count,
                                        int groups) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)count * groups) return;
   const int g = (int)(i / count), t = (int)(i % count);
@@ -506,6 +519,7 @@ __global__ void scales_by_group_kernel(float *dst, int64_t t_stride, const float
 
 __global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                                        const int32_t *channels, int nch) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)vocab * nch) return;
   const int c = (int)(i / vocab), v = (int)(i % vocab);
@@ -514,18 +528,22 @@ __global__ void outlier_columns_kernel(float *cols, const int8_t *w, const float
 }
 
 __global__ void to_f16_kernel(uint16_t *out, const float *x, int64_t n) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = float_to_half(x[i]);
 }
 __global__ void from_f16_kernel(float *out, const uint16_t *x, int64_t n) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = half_to_float(x[i]);
 }
 __global__ void add_inplace_kernel(float *x, const float *y, int64_t n) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) x[i] = fadd(x[i], y[i]);
 }
 __global__ void swiglu_kernel(float *out, const float *h1, const float *h3, int64_t n) {
+  pdl_begin();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = h1[i];
@@ -533,6 +551,7 @@ __global__ void swiglu_kernel(float *out, const float *h1, const float *h3, int6
   out[i] = fmul(fdiv(v, fadd(1.0f, e)), h3[i]);
 }
 __global__ void int8_sums_kernel(int32_t *out, const int8_t *w, int64_t groups) {
+  pdl_begin();
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= groups) return;
   int s = 0;
@@ -541,6 +560,7 @@ __global__ void int8_sums_kernel(int32_t *out, const int8_t *w, int64_t groups) 
 }
 __global__ void advance_kernel(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *history, int steps,
                                int32_t *step, int count, const float *logits, int64_t vocab, int32_t *bad) {
+  pdl_begin();
   const int i = threadIdx.x;
   const int at = *step;
   __syncthreads();
@@ -572,7 +592,7 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
   if (jobs.n % 32) return fail(B200FWD_EINVAL, "matvec: n must be whole groups of 32");
   const unsigned grid = std::min<unsigned>(blocks_for(jobs.total_rows, MV_WARPS), 148u * 32u);
   const int mt = count >= 8 ? 8 : count >= 4 ? 4 : count >= 2 ? 2 : 1;
-#define B200_MV(MT, R) matvec_kernel<MT, R><<<grid, MV_WARPS * 32, 0, stream>>>(jobs, xq, xs, q_stride, s_stride, g_stride, count)
+#define B200_MV(MT, R) launch(matvec_kernel<MT, R>, grid, MV_WARPS * 32, 0, stream, jobs, xq, xs, q_stride, s_stride, g_stride, count)
   if (relaxed) {
     switch (mt) {
       case 8: B200_MV(8, true); break;
@@ -603,7 +623,7 @@ int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n
   // a block per token: the squares and the groups' quantization spread over the block (only the four lane chains of
   // the norm are serial); 1024 threads while the tokens leave SMs free, 256 (more tokens' chains at once) past that
   const int threads = count <= 148 ? 1024 : 256;
-  norm_quantize_kernel<<<count, threads, (size_t)n * 4, stream>>>(x, x_stride, w, n, eps, bias, xq, q_stride, xs,
+  launch(norm_quantize_kernel, count, threads, (size_t)n * 4, stream, x, x_stride, w, n, eps, bias, xq, q_stride, xs,
                                                                   s_stride, g_stride, channels, nch, picked, out_f,
                                                                   out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
@@ -617,13 +637,13 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
   if (count > 65535) return fail(B200FWD_EINVAL, "quantize_x: more than 65535 tokens");
   if (reinterpret_cast<uintptr_t>(x) % 16 == 0 && x_stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 &&
       q_stride % 4 == 0) {
-    quantize_v4_kernel<false><<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(x, nullptr, x_stride, n, bias,
+    launch(quantize_v4_kernel<false>, dim3(blocks_for(n / 32, 32), count), 256, 0, stream, x, nullptr, x_stride, n, bias,
                                                                                        xq, q_stride, xs, s_stride,
                                                                                        g_stride, shift);
     B200_LAUNCHED("quantize_v4_kernel");
     return 0;
   }
-  quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(x, x_stride, n, bias, count, xq, q_stride,
+  launch(quantize_kernel, dim3(blocks_for(n / 32, 8), count), 256, 0, stream, x, x_stride, n, bias, count, xq, q_stride,
                                                                           xs, s_stride, g_stride, shift);
   B200_LAUNCHED("quantize_kernel");
   return 0;
@@ -638,13 +658,13 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
   const bool v4 = reinterpret_cast<uintptr_t>(h1) % 16 == 0 && reinterpret_cast<uintptr_t>(h3) % 16 == 0 &&
                   stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 && q_stride % 4 == 0;
   if (v4) {
-    quantize_v4_kernel<true><<<dim3(blocks_for(n / 32, 32), count), 256, 0, stream>>>(h1, h3, stride, n, bias, xq,
+    launch(quantize_v4_kernel<true>, dim3(blocks_for(n / 32, 32), count), 256, 0, stream, h1, h3, stride, n, bias, xq,
                                                                                       q_stride, xs, s_stride,
                                                                                       g_stride, shift);
     B200_LAUNCHED("quantize_v4_kernel<swiglu>");
     return 0;
   }
-  swiglu_quantize_kernel<<<dim3(blocks_for(n / 32, 8), count), 256, 0, stream>>>(h1, h3, stride, n, bias, count, xq,
+  launch(swiglu_quantize_kernel, dim3(blocks_for(n / 32, 8), count), 256, 0, stream, h1, h3, stride, n, bias, count, xq,
                                                                                  q_stride, xs, s_stride, g_stride,
                                                                                  shift);
   B200_LAUNCHED("swiglu_quantize_kernel");
@@ -654,7 +674,7 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
 int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim, float *x,
                  int64_t x_stride, cudaStream_t stream) {
   if (count <= 0) return 0;
-  embed_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(w, s, sstride, tokens, count, dim, x,
+  launch(embed_kernel, blocks_for((int64_t)count * dim, 256), 256, 0, stream, w, s, sstride, tokens, count, dim, x,
                                                                           x_stride);
   B200_LAUNCHED("embed_kernel");
   return 0;
@@ -667,7 +687,7 @@ int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v
   if (hs % 2) return fail(B200FWD_EINVAL, "rope: the head size must be even");
   const int total = (nh + nkv) * (hs / 2) + nkv * hs;
   dim3 grid(blocks_for(total, 256), count);
-  rope_cache_kernel<<<grid, 256, 0, stream>>>(q, q_stride, k, v, kv_stride, cos, sin, pos, seq,
+  launch(rope_cache_kernel, grid, 256, 0, stream, q, q_stride, k, v, kv_stride, cos, sin, pos, seq,
                                               reinterpret_cast<uint8_t *>(kc), reinterpret_cast<uint8_t *>(vc),
                                               seq_stride, half, nh, nkv, hs, rot);
   B200_LAUNCHED("rope_cache_kernel");
@@ -678,7 +698,7 @@ int launch_rmsnorm(float *out, const float *x, const float *w, int n, float eps,
                    cudaStream_t stream) {
   if (count <= 0) return 0;
   if (n > NORM_MAX) return fail(B200FWD_EUNSUPPORTED, "rmsnorm: vectors above 12288 values");
-  rmsnorm_kernel<<<count, 256, (size_t)n * 4, stream>>>(out, x, w, n, eps, stride);
+  launch(rmsnorm_kernel, count, 256, (size_t)n * 4, stream, out, x, w, n, eps, stride);
   B200_LAUNCHED("rmsnorm_kernel");
   return 0;
 }
@@ -687,7 +707,7 @@ int launch_rope(float *v, const float *fcr, const float *fci, int nh, int hs, in
   const int turned = rot > 0 && rot < hs ? rot : hs;
   const int pairs = nh * (turned / 2);
   if (pairs <= 0) return 0;
-  rope_kernel<<<blocks_for(pairs, 128), 128, 0, stream>>>(v, fcr, fci, nh, hs, rot);
+  launch(rope_kernel, blocks_for(pairs, 128), 128, 0, stream, v, fcr, fci, nh, hs, rot);
   B200_LAUNCHED("rope_kernel");
   return 0;
 }
@@ -695,7 +715,7 @@ int launch_rope(float *v, const float *fcr, const float *fci, int nh, int hs, in
 int launch_add_columns(float *y, int64_t y_stride, const float *rows, const float *a, int64_t a_stride, int nc,
                        int n, int count, cudaStream_t stream) {
   if (count <= 0 || nc <= 0) return 0;
-  add_columns_kernel<<<blocks_for((int64_t)n * count, 256), 256, 0, stream>>>(y, y_stride, rows, a, a_stride, nc, n,
+  launch(add_columns_kernel, blocks_for((int64_t)n * count, 256), 256, 0, stream, y, y_stride, rows, a, a_stride, nc, n,
                                                                              count);
   B200_LAUNCHED("add_columns_kernel");
   return 0;
@@ -703,7 +723,7 @@ int launch_add_columns(float *y, int64_t y_stride, const float *rows, const floa
 
 int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count, int mode, cudaStream_t stream) {
   if (count <= 0) return 0;
-  argmax_kernel<<<count, 1024, 0, stream>>>(out, x, stride, n, mode);
+  launch(argmax_kernel, count, 1024, 0, stream, out, x, stride, n, mode);
   B200_LAUNCHED("argmax_kernel");
   return 0;
 }
@@ -711,7 +731,7 @@ int launch_argmax(int32_t *out, const float *x, int64_t stride, int n, int count
 int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t src_stride, const int32_t *idx,
                        int count, int dim, cudaStream_t stream) {
   if (count <= 0) return 0;
-  gather_rows_kernel<<<blocks_for((int64_t)count * dim, 256), 256, 0, stream>>>(dst, dst_stride, src, src_stride,
+  launch(gather_rows_kernel, blocks_for((int64_t)count * dim, 256), 256, 0, stream, dst, dst_stride, src, src_stride,
                                                                                 idx, count, dim);
   B200_LAUNCHED("gather_rows_kernel");
   return 0;
@@ -720,7 +740,7 @@ int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t
 int launch_scales_by_group(float *dst, int64_t t_stride, const float *src, int64_t s_stride, int count, int groups,
                            cudaStream_t stream) {
   if (count <= 0 || groups <= 0) return 0;
-  scales_by_group_kernel<<<blocks_for((int64_t)count * groups, 256), 256, 0, stream>>>(dst, t_stride, src, s_stride,
+  launch(scales_by_group_kernel, blocks_for((int64_t)count * groups, 256), 256, 0, stream, dst, t_stride, src, s_stride,
                                                                                       count, groups);
   B200_LAUNCHED("scales_by_group_kernel");
   return 0;
@@ -729,7 +749,7 @@ int launch_scales_by_group(float *dst, int64_t t_stride, const float *src, int64
 int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int sstride, int dim, int vocab,
                            const int32_t *channels, int nch, cudaStream_t stream) {
   if (nch <= 0) return 0;
-  outlier_columns_kernel<<<blocks_for((int64_t)vocab * nch, 256), 256, 0, stream>>>(cols, w, s, sstride, dim, vocab,
+  launch(outlier_columns_kernel, blocks_for((int64_t)vocab * nch, 256), 256, 0, stream, cols, w, s, sstride, dim, vocab,
                                                                                      channels, nch);
   B200_LAUNCHED("outlier_columns_kernel");
   return 0;
@@ -737,31 +757,31 @@ int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int sst
 
 int launch_to_f16(uint16_t *out, const float *x, int64_t n, cudaStream_t stream) {
   if (n <= 0) return 0;
-  to_f16_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, x, n);
+  launch(to_f16_kernel, blocks_for(n, 256), 256, 0, stream, out, x, n);
   B200_LAUNCHED("to_f16_kernel");
   return 0;
 }
 int launch_from_f16(float *out, const uint16_t *x, int64_t n, cudaStream_t stream) {
   if (n <= 0) return 0;
-  from_f16_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, x, n);
+  launch(from_f16_kernel, blocks_for(n, 256), 256, 0, stream, out, x, n);
   B200_LAUNCHED("from_f16_kernel");
   return 0;
 }
 int launch_add_inplace(float *x, const float *y, int64_t n, cudaStream_t stream) {
   if (n <= 0) return 0;
-  add_inplace_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(x, y, n);
+  launch(add_inplace_kernel, blocks_for(n, 256), 256, 0, stream, x, y, n);
   B200_LAUNCHED("add_inplace_kernel");
   return 0;
 }
 int launch_swiglu(float *out, const float *h1, const float *h3, int64_t n, cudaStream_t stream) {
   if (n <= 0) return 0;
-  swiglu_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(out, h1, h3, n);
+  launch(swiglu_kernel, blocks_for(n, 256), 256, 0, stream, out, h1, h3, n);
   B200_LAUNCHED("swiglu_kernel");
   return 0;
 }
 int launch_int8_sums(int32_t *out, const int8_t *w, int64_t groups, cudaStream_t stream) {
   if (groups <= 0) return 0;
-  int8_sums_kernel<<<blocks_for(groups, 256), 256, 0, stream>>>(out, w, groups);
+  launch(int8_sums_kernel, blocks_for(groups, 256), 256, 0, stream, out, w, groups);
   B200_LAUNCHED("int8_sums_kernel");
   return 0;
 }
@@ -769,7 +789,7 @@ int launch_advance(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *h
                    int count, const float *logits, int64_t vocab, int32_t *bad, cudaStream_t stream) {
   if (count <= 0) return 0;
   if (count > 1024) return fail(B200FWD_EINVAL, "advance: more than 1024 sequences");
-  advance_kernel<<<1, ((count + 31) / 32) * 32, 0, stream>>>(tokens, pos, ids, history, steps, step, count, logits,
+  launch(advance_kernel, 1, ((count + 31) / 32) * 32, 0, stream, tokens, pos, ids, history, steps, step, count, logits,
                                                              vocab, bad);
   B200_LAUNCHED("advance_kernel");
   return 0;

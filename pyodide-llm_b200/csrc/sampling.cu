@@ -160,6 +160,7 @@ __device__ bool sort_nucleus(float *probs, int32_t *index, int lo, int hi, doubl
 // each token made less likely once. Sequences with done[s] are left alone.
 __global__ void penalize_kernel(float *logits, int64_t stride, const int32_t *recent, int window,
                                 const int32_t *recent_count, float penalty, const int32_t *done) {
+  pdl_begin();
   const int s = blockIdx.x;
   if (done && done[s]) return;
   const int count = recent_count ? min(recent_count[s], window) : window;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(ST)
     sample_kernel(int32_t *out, const float *logits, int64_t stride, int n, float temperature, float topp,
                   const double *random, double random0, int64_t rstride, const int32_t *step, float *scratch,
                   int32_t *stacks, const int32_t *done) {
+  pdl_begin();
   __shared__ float fred[32];
   __shared__ int ired[33];
   __shared__ double shared_total;
@@ -303,6 +305,7 @@ __global__ void advance_sampled_kernel(int32_t *tokens, int32_t *pos, const int3
                                        int steps, int32_t *step, int count, const float *logits, int64_t vocab,
                                        int greedy, int32_t *recent, int window, int32_t *recent_count,
                                        const int32_t *stops, int nstops, int32_t *done, int32_t *made, int32_t *bad) {
+  pdl_begin();
   const int i = threadIdx.x;
   const int atstep = *step;
   __syncthreads();
@@ -341,7 +344,7 @@ size_t sample_stack_words() { return (size_t)3 * STACK_FRAMES; }
 int launch_penalize(float *logits, int64_t stride, const int32_t *recent, int window, const int32_t *recent_count,
                     float penalty, const int32_t *done, int count, cudaStream_t stream) {
   if (count <= 0) return 0;
-  penalize_kernel<<<count, 64, 0, stream>>>(logits, stride, recent, window, recent_count, penalty, done);
+  launch(penalize_kernel, count, 64, 0, stream, logits, stride, recent, window, recent_count, penalty, done);
   B200_LAUNCHED("penalize_kernel");
   return 0;
 }
@@ -352,7 +355,7 @@ int launch_sample(int32_t *out, const float *logits, int64_t stride, int n, floa
   if (count <= 0) return 0;
   if (n < 1) return fail(B200FWD_EINVAL, "sample: no logits");
   if (!(temperature > 0)) return fail(B200FWD_EINVAL, "sample: the temperature must be above 0 (0 is greedy)");
-  sample_kernel<<<count, ST, 0, stream>>>(out, logits, stride, n, temperature, topp, random, random0, rstride, step,
+  launch(sample_kernel, count, ST, 0, stream, out, logits, stride, n, temperature, topp, random, random0, rstride, step,
                                           scratch, stacks, done);
   B200_LAUNCHED("sample_kernel");
   return 0;
@@ -363,7 +366,7 @@ int launch_advance_sampled(int32_t *tokens, int32_t *pos, const int32_t *ids, in
                            int window, int32_t *recent_count, const int32_t *stops, int nstops, int32_t *done,
                            int32_t *made, int32_t *bad, cudaStream_t stream) {
   if (count > 1024) return fail(B200FWD_EINVAL, "sampled steps: at most 1024 sequences at once");
-  advance_sampled_kernel<<<1, ((count + 31) / 32) * 32, 0, stream>>>(tokens, pos, ids, history, steps, step, count,
+  launch(advance_sampled_kernel, 1, ((count + 31) / 32) * 32, 0, stream, tokens, pos, ids, history, steps, step, count,
                                                                      logits, vocab, greedy, recent, window,
                                                                      recent_count, stops, nstops, done, made, bad);
   B200_LAUNCHED("advance_sampled_kernel");

@@ -216,6 +216,13 @@ __device__ __forceinline__ void tmem_ld_16x256_x2(uint32_t taddr, uint32_t (&r)[
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
+// the loads issued so far have landed; r (the last one's registers) is read only after this
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
+               :
+               : "memory");
+}
 
 __device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) { return (uint64_t)lo | ((uint64_t)hi << 32); }
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
@@ -266,35 +273,56 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
       tc_fence_after();
       const float *wq = &s.ws[st][quarter * 32 + rq][0];  // row rq + 8i's group j: wq[32 * i + j]
       const float *xq = s.xs[st] + sub * 16 + 2 * c;      // group j's token pair p: xq[j * BN + 8 * p], two floats
-      const bool whole = !TAIL || 4 * k + 4 <= ng4;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        uint32_t v[2][8];  // the two 16-lane halves' fragments
+      if (!TAIL || 4 * k + 4 <= ng4) {
+        // four whole groups. Step q = 2j + h works on group j's half h (rows rq + 8i, i = 2h, 2h + 1): it waits for
+        // its own TMEM load, issues the next step's, then computes, so that each load lands during a step's work.
+        // Row rq + 8i, pair p: fragment registers 4p + 2(i & 1), +1.
+        uint32_t v[2][8];
         uint32_t wv[4];
         uint64_t x2[2];
-        if (j < groups) {
-          const uint32_t col = (uint32_t)((slot * 4 + j) * BN);
-          tmem_ld_16x256_x2(t_lo + col, v[0]);
-          tmem_ld_16x256_x2(t_hi + col, v[1]);
+        tmem_ld_16x256_x2(t_lo + (uint32_t)(slot * 4 * BN), v[0]);
 #pragma unroll
-          for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+        for (int q = 0; q < 8; q++) {
+          const int j = q >> 1, h = q & 1;
+          tmem_wait_ld(v[q & 1]);
+          if (q < 7)
+            tmem_ld_16x256_x2(((q + 1) & 1 ? t_hi : t_lo) + (uint32_t)((slot * 4 + ((q + 1) >> 1)) * BN),
+                              v[(q + 1) & 1]);
+          if (h == 0) {
 #pragma unroll
-          for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
-          tmem_wait_ld();
-        }
-        // row rq + 8i, pair p: fragment registers 4p + 2(i & 1), +1 of half i >> 1
-        if (whole) {
+            for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+#pragma unroll
+            for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
+          }
           // lane j of the chain takes group 4k + j: float(S) x (weight scale x activation scale), rounded once each
           // (kernel_relaxed.ts:45,55), added into the lane
 #pragma unroll
-          for (int i = 0; i < 4; i++)
+          for (int ii = 0; ii < 2; ii++) {
+            const int i = 2 * h + ii;
 #pragma unroll
             for (int p = 0; p < 2; p++) {
-              const int r = 4 * p + 2 * (i & 1);
-              const uint64_t sums = pk2(v[i >> 1][r], v[i >> 1][r + 1]);
+              const int r = 4 * p + 2 * ii;
+              const uint64_t sums = pk2(v[q & 1][r], v[q & 1][r + 1]);
               acc[i][p][j] = fma2(one2, acc[i][p][j], mul2(sums, mul2(pk2(wv[i], wv[i]), x2[p])));
             }
-        } else {
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          uint32_t v[2][8];  // the two 16-lane halves' fragments
+          uint32_t wv[4];
+          uint64_t x2[2];
+          if (j < groups) {
+            const uint32_t col = (uint32_t)((slot * 4 + j) * BN);
+            tmem_ld_16x256_x2(t_lo + col, v[0]);
+            tmem_ld_16x256_x2(t_hi + col, v[1]);
+#pragma unroll
+            for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+#pragma unroll
+            for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
+            tmem_wait_ld();
+          }
           // the stage of the groups past the fours (kernel_relaxed.ts:57-64): the lanes added in order first (kept in
           // lane 0), then each group in turn
 #pragma unroll

@@ -94,7 +94,9 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     B200_CUDA(cudaGetSymbolAddress((void **)&err, capi_tc_error));
     const int sms = gemm_sms();
     if (sms < 0) return sms;
-    const int bn = choose_gemm_bn(rows, count, sms, 64);
+    // the token maps hold exactly `count` rows: tiles no wider than the tokens (past 16)
+    const int widest = count >= 64 ? 64 : count >= 32 ? 32 : 16;
+    const int bn = choose_gemm_bn(rows, count, sms, widest);
     // the kernel reads the activation scales one row per group: a stream-ordered copy in that layout
     const int64_t tstride = (count + 3) / 4 * 4;
     float *xs_g = nullptr;
@@ -117,9 +119,9 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     a.out_stride = out_stride;
     a.accumulate = 0;
     GemmMaps maps;
-    if (!rc && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) && gemm_lanes_pays(rows, count, sms)) {
+    if (!rc && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) && gemm_lanes_pays(rows, count, n, sms, widest)) {
       // n a multiple of 128 and few row tiles: the lane-split kernel (a cluster of four CTAs per tile)
-      const int lbn = choose_lanes_bn(count, count >= 64 ? 64 : count >= 32 ? 32 : 16);
+      const int lbn = choose_lanes_bn(count, widest);
       rc = make_lane_weight_maps(&maps.w, &maps.ws, wq, ws, n, rows, ws_stride);
       if (!rc) rc = make_lane_token_maps(&maps.x, &maps.xs, xq, xs_g, count, q_stride, n, tstride, lbn);
       if (!rc) rc = launch_gemm_lanes(maps, a, lbn, st);

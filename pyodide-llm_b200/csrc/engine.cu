@@ -344,7 +344,8 @@ int matmul(b200fwd_engine *e, const Matrix &m, int layer, float *out, int64_t ou
     a.w_row0 = layer * m.rows;
     a.out_stride = out_stride;
     a.accumulate = accumulate;
-    if (e->lanes && m.lane_mapped && gemm_lanes_fits(m.n, m.rows, count) && gemm_lanes_pays(m.rows, count, e->sms)) {
+    if (e->lanes && m.lane_mapped && gemm_lanes_fits(m.n, m.rows, count) &&
+        gemm_lanes_pays(m.rows, count, m.n, e->sms, e->widest_tile)) {
       const int bn = choose_lanes_bn(count, 64);
       const int which = bn == 16 ? 0 : bn == 32 ? 1 : 2;
       GemmMaps maps{m.lwmap, e->lxmap[which], m.lsmap, e->lxsmap[which]};

@@ -84,6 +84,125 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
+// The epilogue of 64- and 32-token tiles. Epilogue warp w reads TMEM lane quarter w % 4 and token columns
+// (w - 4) / 4 * TPW .. + TPW as 16x256b fragments of both 16-lane halves, so that thread t keeps chain `rank` of four
+// rows (quarter * 32 + t/4 + 8i) x PP = BN / 32 token pairs (8p + 2(t%4), +1 of the warp's TPW): each activation-scale
+// pair read from shared memory serves four rows, and a pair's two tokens (adjacent in the fragment) go through each
+// float operation together. At the end of a tile the warp hands its values to the same warp of CTA `sub`, which holds
+// the same (row, token) pairs of the other chains and adds the four lanes in order.
+template <int BN>
+__device__ __forceinline__ void lanes_epilogue_4x4(LSmem<BN> &s, uint32_t tmem, int quarter, int sub, int lane,
+                                                   int rank, int cid, int ncl, const GemmArgs &args, int tiles,
+                                                   int ntok, int kstages, int nquads, float one) {
+  constexpr int STAGES = LTile<BN>::STAGES, SLOTS = LTile<BN>::SLOTS, TPW = LTile<BN>::TPW, PP = BN / 32;
+  constexpr int NP = 4 * PP;  // the (row, token pair) pairs of a thread: n = i * PP + p
+  const int c = lane & 3, rq = lane >> 2;
+  const uint32_t t_lo = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW), t_hi = t_lo + (16u << 16);
+  const uint64_t one2 = pk2(__float_as_uint(one), __float_as_uint(one));
+  Ring<STAGES> ring;
+  Ring<SLOTS> slots;
+  int iter = 0;
+  for (int tile = cid; tile < tiles; tile += ncl, iter++) {
+    const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+    uint64_t acc[NP];  // chain `rank` of row rq + 8i, tokens 8p + 2c, +1
+#pragma unroll
+    for (int n = 0; n < NP; n++) acc[n] = 0;
+    for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+      const int st = ring.i, slot = slots.i;
+      mbar_wait(&s.full[st], ring.phase, args.error, 14);
+      mbar_wait(&s.slot_full[slot], slots.phase, args.error, 15);
+      fence_after();
+      uint32_t v[4][2][4 * PP];  // quad, 16-lane half
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        tmem_ld_16x256<PP>(t_lo + (uint32_t)((slot * 4 + q) * BN), v[q][0]);
+        tmem_ld_16x256<PP>(t_hi + (uint32_t)((slot * 4 + q) * BN), v[q][1]);
+      }
+      tmem_wait_ld();
+      // the slot is in registers: back to the MMAs before the arithmetic
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
+      const int quads = min(4, nquads - 4 * k);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        if (q < quads) {
+          // group 16k + 4q + rank: float(S) x (weight scale x activation scale), rounded once each
+          // (kernel_relaxed.ts:45,55), added into the chain
+          const float *wq = &s.ws[st][q][quarter * 32 + rq][rank];  // row rq + 8i: wq[32 * i]
+          const float *xq = s.xs[st][q] + sub * TPW + 2 * c;       // token pair p: xq[8p], two floats
+          uint64_t x2[PP];
+#pragma unroll
+          for (int p = 0; p < PP; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + 8 * p);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const uint32_t w = __float_as_uint(wq[32 * i]);
+            const uint64_t w2 = pk2(w, w);
+#pragma unroll
+            for (int p = 0; p < PP; p++) {
+              const int r = 4 * p + 2 * (i & 1);
+              acc[i * PP + p] = fma2(one2, acc[i * PP + p],
+                                     mul2(pk2(v[q][i >> 1][r], v[q][i >> 1][r + 1]), mul2(w2, x2[p])));
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[st]);
+    }
+    // ---- the four chains of this warp's (row, token) pairs meet in the same warp of CTA `sub`: a source's values at
+    // [quarter][v4 k][lane] of its slot, four floats (pairs 2k, 2k + 1) each
+    const int b = iter & 1;
+    if (sub != rank) {
+      const int from = rank < sub ? rank : rank - 1;
+      const uint32_t dst =
+          cluster_map(&s.xbuf[b][from][0][0], (uint32_t)sub) + (uint32_t)(quarter * (NP / 2) * 32 * 16);
+#pragma unroll
+      for (int k4 = 0; k4 < NP / 2; k4++)
+        st_cluster_v4(dst + (uint32_t)((k4 * 32 + lane) * 16), lo_f(acc[2 * k4]), hi_f(acc[2 * k4]),
+                      lo_f(acc[2 * k4 + 1]), hi_f(acc[2 * k4 + 1]));
+      mbar_arrive_cluster(cluster_map(&s.xfull[b], (uint32_t)sub));
+    } else {
+      const bool ok = mbar_wait<true>(&s.xfull[b], (iter >> 1) & 1, args.error, 18);
+      if (ok) {
+#pragma unroll
+        for (int k4 = 0; k4 < NP / 2; k4++) {
+          float4 o[LANES - 1];
+#pragma unroll
+          for (int f = 0; f < LANES - 1; f++)
+            o[f] = reinterpret_cast<const float4 *>(&s.xbuf[b][f][0][0])[(quarter * (NP / 2) + k4) * 32 + lane];
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const int n = 2 * k4 + h, i = n / PP, p = n % PP;
+            const int r = row0 + quarter * 32 + rq + 8 * i;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+              const int comp = 2 * h + e;
+              float l[LANES];
+#pragma unroll
+              for (int j = 0; j < LANES; j++) {
+                if (j == rank) {
+                  l[j] = e ? hi_f(acc[n]) : lo_f(acc[n]);
+                } else {
+                  const float4 &src = o[j < rank ? j : j - 1];
+                  l[j] = comp == 0 ? src.x : comp == 1 ? src.y : comp == 2 ? src.z : src.w;
+                }
+              }
+              // kernel_relaxed.ts:57: ((lane 0 + lane 1) + lane 2) + lane 3
+              const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[1]), l[2]), l[3]);
+              const int tok = tok0 + sub * TPW + 8 * p + 2 * c + e;
+              if (r < args.rows && tok < args.count) {
+                float *out = args.out + (int64_t)tok * args.out_stride + r;
+                *out = args.accumulate ? __fadd_rn(*out, sum) : sum;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int BN>
 __global__ void __cluster_dims__(LANES, 1, 1) __launch_bounds__(THREADS, 1)
     q8_gemm_lanes(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
@@ -199,79 +318,83 @@ __global__ void __cluster_dims__(LANES, 1, 1) __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
     // ---- epilogue: warp (quarter, sub) reads TMEM lanes quarter * 32.. (its rows) and tokens sub * TPW.. + TPW
     const int quarter = warp % 4, sub = (warp - EPI_WARP0) / 4;
-    const int rl = quarter * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
-    const uint64_t one2 = pk2(__float_as_uint(one), __float_as_uint(one));
-    Ring<STAGES> ring;
-    Ring<SLOTS> slots;
-    int iter = 0;
-    for (int tile = cid; tile < tiles; tile += ncl, iter++) {
-      const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
-      uint64_t acc[TPW / 2];  // chain `rank` of tokens 2p, 2p + 1
+    if constexpr (BN >= 32) {
+      lanes_epilogue_4x4<BN>(s, tmem, quarter, sub, lane, rank, cid, ncl, args, tiles, ntok, kstages, nquads, one);
+    } else {
+      const int rl = quarter * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
+      const uint64_t one2 = pk2(__float_as_uint(one), __float_as_uint(one));
+      Ring<STAGES> ring;
+      Ring<SLOTS> slots;
+      int iter = 0;
+      for (int tile = cid; tile < tiles; tile += ncl, iter++) {
+        const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
+        uint64_t acc[TPW / 2];  // chain `rank` of tokens 2p, 2p + 1
 #pragma unroll
-      for (int p = 0; p < TPW / 2; p++) acc[p] = 0;
-      for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
-        const int st = ring.i, slot = slots.i;
-        mbar_wait(&s.full[st], ring.phase, args.error, 14);
-        mbar_wait(&s.slot_full[slot], slots.phase, args.error, 15);
-        fence_after();
-        uint32_t v[4][TPW];
+        for (int p = 0; p < TPW / 2; p++) acc[p] = 0;
+        for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
+          const int st = ring.i, slot = slots.i;
+          mbar_wait(&s.full[st], ring.phase, args.error, 14);
+          mbar_wait(&s.slot_full[slot], slots.phase, args.error, 15);
+          fence_after();
+          uint32_t v[4][TPW];
 #pragma unroll
-        for (int q = 0; q < 4; q++) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + q) * BN), v[q]);
-        tmem_wait_ld();
-        // the slot is in registers: back to the MMAs before the arithmetic
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
-        const int quads = min(4, nquads - 4 * k);
+          for (int q = 0; q < 4; q++) tmem_ld<TPW>(taddr + (uint32_t)((slot * 4 + q) * BN), v[q]);
+          tmem_wait_ld();
+          // the slot is in registers: back to the MMAs before the arithmetic
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.slot_empty[slot]);
+          const int quads = min(4, nquads - 4 * k);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          if (q < quads) {
-            // group 16k + 4q + rank: float(S) x (weight scale x activation scale), rounded once each
-            // (kernel_relaxed.ts:45,55), added into the chain
-            const uint32_t w = __float_as_uint(s.ws[st][q][rl][rank]);
-            const uint64_t w2 = pk2(w, w);
-            const float *xrow = s.xs[st][q] + sub * TPW;
+          for (int q = 0; q < 4; q++) {
+            if (q < quads) {
+              // group 16k + 4q + rank: float(S) x (weight scale x activation scale), rounded once each
+              // (kernel_relaxed.ts:45,55), added into the chain
+              const uint32_t w = __float_as_uint(s.ws[st][q][rl][rank]);
+              const uint64_t w2 = pk2(w, w);
+              const float *xrow = s.xs[st][q] + sub * TPW;
 #pragma unroll
-            for (int p4 = 0; p4 < TPW / 4; p4++) {
-              const uint4 x4 = *reinterpret_cast<const uint4 *>(xrow + 4 * p4);
-              acc[2 * p4] = fma2(one2, acc[2 * p4],
-                                 mul2(pk2(v[q][4 * p4], v[q][4 * p4 + 1]), mul2(w2, pk2(x4.x, x4.y))));
-              acc[2 * p4 + 1] = fma2(one2, acc[2 * p4 + 1],
-                                     mul2(pk2(v[q][4 * p4 + 2], v[q][4 * p4 + 3]), mul2(w2, pk2(x4.z, x4.w))));
+              for (int p4 = 0; p4 < TPW / 4; p4++) {
+                const uint4 x4 = *reinterpret_cast<const uint4 *>(xrow + 4 * p4);
+                acc[2 * p4] = fma2(one2, acc[2 * p4],
+                                   mul2(pk2(v[q][4 * p4], v[q][4 * p4 + 1]), mul2(w2, pk2(x4.x, x4.y))));
+                acc[2 * p4 + 1] = fma2(one2, acc[2 * p4 + 1],
+                                       mul2(pk2(v[q][4 * p4 + 2], v[q][4 * p4 + 3]), mul2(w2, pk2(x4.z, x4.w))));
+              }
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.empty[st]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s.empty[st]);
-      }
-      // ---- the four chains of this warp's (row, token) pairs meet in CTA `sub`
-      const int b = iter & 1;
-      if (sub != rank) {
-        const int from = rank < sub ? rank : rank - 1;
-        const uint32_t dst = cluster_map(&s.xbuf[b][from][rl][0], (uint32_t)sub);
+        // ---- the four chains of this warp's (row, token) pairs meet in CTA `sub`
+        const int b = iter & 1;
+        if (sub != rank) {
+          const int from = rank < sub ? rank : rank - 1;
+          const uint32_t dst = cluster_map(&s.xbuf[b][from][rl][0], (uint32_t)sub);
 #pragma unroll
-        for (int p4 = 0; p4 < TPW / 4; p4++)
-          st_cluster_v4(dst + 16 * p4, lo_f(acc[2 * p4]), hi_f(acc[2 * p4]), lo_f(acc[2 * p4 + 1]),
-                        hi_f(acc[2 * p4 + 1]));
-        mbar_arrive_cluster(cluster_map(&s.xfull[b], (uint32_t)sub));
-      } else {
-        const bool ok = mbar_wait<true>(&s.xfull[b], (iter >> 1) & 1, args.error, 18);
-        const int r = row0 + rl;
-        if (ok && r < args.rows) {
+          for (int p4 = 0; p4 < TPW / 4; p4++)
+            st_cluster_v4(dst + 16 * p4, lo_f(acc[2 * p4]), hi_f(acc[2 * p4]), lo_f(acc[2 * p4 + 1]),
+                          hi_f(acc[2 * p4 + 1]));
+          mbar_arrive_cluster(cluster_map(&s.xfull[b], (uint32_t)sub));
+        } else {
+          const bool ok = mbar_wait<true>(&s.xfull[b], (iter >> 1) & 1, args.error, 18);
+          const int r = row0 + rl;
+          if (ok && r < args.rows) {
 #pragma unroll
-          for (int t = 0; t < TPW; t++) {
-            const int tok = tok0 + sub * TPW + t;
-            const float mine = (t & 1) ? hi_f(acc[t >> 1]) : lo_f(acc[t >> 1]);
-            float l[LANES];
+            for (int t = 0; t < TPW; t++) {
+              const int tok = tok0 + sub * TPW + t;
+              const float mine = (t & 1) ? hi_f(acc[t >> 1]) : lo_f(acc[t >> 1]);
+              float l[LANES];
 #pragma unroll
-            for (int j = 0; j < LANES; j++)
-              l[j] = j == rank ? mine : s.xbuf[b][j < rank ? j : j - 1][rl][t];
-            // kernel_relaxed.ts:57: ((lane 0 + lane 1) + lane 2) + lane 3
-            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[1]), l[2]), l[3]);
-            if (tok < args.count) {
-              float *o = args.out + (int64_t)tok * args.out_stride + r;
-              *o = args.accumulate ? __fadd_rn(*o, sum) : sum;
+              for (int j = 0; j < LANES; j++)
+                l[j] = j == rank ? mine : s.xbuf[b][j < rank ? j : j - 1][rl][t];
+              // kernel_relaxed.ts:57: ((lane 0 + lane 1) + lane 2) + lane 3
+              const float sum = __fadd_rn(__fadd_rn(__fadd_rn(l[0], l[1]), l[2]), l[3]);
+              if (tok < args.count) {
+                float *o = args.out + (int64_t)tok * args.out_stride + r;
+                *o = args.accumulate ? __fadd_rn(*o, sum) : sum;
+              }
             }
           }
         }
@@ -394,11 +517,27 @@ bool gemm_lanes_fits(int n, int rows, int count) {
   return n % 128 == 0 && n / 128 >= 16 && rows >= BM && count > 0;
 }
 
-bool gemm_lanes_pays(int rows, int count, int sms) {
-  // measured (64 and 8 tokens, the 8B shapes): four CTAs a tile win while the split tiles still fit the SMs in one
-  // round (w2 and wo: 32 row tiles); with more row tiles the one-CTA kernel is as fast or faster
-  const int64_t tiles = (int64_t)((rows + BM - 1) / BM) * ((count + 63) / 64);
-  return LANES * tiles <= sms;
+// time of a stage of one lane (four quads of K) by tile width, in hundredths of a microsecond at 1965 MHz, and the
+// kernel's fixed cost: measured on the 8B shapes
+constexpr int LANES_STAGE_CUS[3] = {81, 96, 140};
+constexpr int LANES_FIXED_CUS = 300;
+
+bool gemm_lanes_pays(int rows, int count, int n, int sms, int widest) {
+  // B200FWD_GEMM_LANES=2 takes the lane-split kernel wherever it fits (a tuning knob for measurements)
+  static const bool forced = [] {
+    const char *v = getenv("B200FWD_GEMM_LANES");
+    return v && v[0] == '2';
+  }();
+  if (forced) return true;
+  // a cluster of four CTAs takes a tile at a time: rounds of tiles over the clusters, a quarter of K's stages each
+  const int lbn = choose_lanes_bn(count, widest);
+  const int64_t tiles = (int64_t)((rows + BM - 1) / BM) * ((count + lbn - 1) / lbn);
+  const int64_t clusters = std::max(1, sms / LANES);
+  const int64_t lanes = (tiles + clusters - 1) / clusters * ((n / 128 + 3) / 4) *
+                            LANES_STAGE_CUS[lbn == 16 ? 0 : lbn == 32 ? 1 : 2] +
+                        LANES_FIXED_CUS;
+  const int bn = choose_gemm_bn(rows, count, sms, widest);
+  return lanes < gemm_tc_cost(rows, count, n, sms, bn);
 }
 
 int choose_lanes_bn(int count, int widest) {

@@ -192,15 +192,9 @@ struct Smem {
   uint32_t tmem_base;
 };
 
-// TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes (tiles of 16 and 32 tokens)
+// TPW consecutive TMEM columns (the tokens of this warp) of its 32 lanes (tiles of 16 tokens)
 template <int TPW>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[TPW]);
-template <>
-__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
 template <>
 __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
@@ -208,20 +202,35 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
-// 16 TMEM lanes x 16 columns (two 256-bit repetitions) from lane taddr.lane: thread t holds lane t/4 in r[0], r[1]
-// (columns 2(t%4), +1) and r[4], r[5] (columns 8 + 2(t%4), +1), and lane t/4 + 8 in r[2], r[3] and r[6], r[7] (the same
-// columns)
-__device__ __forceinline__ void tmem_ld_16x256_x2(uint32_t taddr, uint32_t (&r)[8]) {
+// 16 TMEM lanes x 8PP columns (PP 256-bit repetitions) from lane taddr.lane: thread t holds lane t/4 in r[4p], r[4p + 1]
+// (columns 8p + 2(t%4), +1) and lane t/4 + 8 in r[4p + 2], r[4p + 3] (the same columns)
+template <int PP>
+__device__ __forceinline__ void tmem_ld_16x256(uint32_t taddr, uint32_t (&r)[4 * PP]);
+template <>
+__device__ __forceinline__ void tmem_ld_16x256<2>(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                : "r"(taddr));
 }
+template <>
+__device__ __forceinline__ void tmem_ld_16x256<1>(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
 // the loads issued so far have landed; r (the last one's registers) is read only after this
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[8]) {
+template <int PP>
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[4 * PP]);
+template <>
+__device__ __forceinline__ void tmem_wait_ld<2>(uint32_t (&r)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
                :
                : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_wait_ld<1>(uint32_t (&r)[4]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]) : : "memory");
 }
 
 __device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) { return (uint64_t)lo | ((uint64_t)hi << 32); }
@@ -239,30 +248,30 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
 __device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
 
-// The epilogue of 64-token tiles. Epilogue warp w reads TMEM lane quarter w % 4 and token columns (w - 4) / 4 * 16 ..
-// + 16 as 16x256b fragments of both 16-lane halves, so that thread t keeps four rows (quarter * 32 + t/4 + 8i) x two
-// token pairs (8p + 2(t%4), +1 of the warp's sixteen). Each activation-scale pair a thread reads from shared memory
-// then serves four rows (against one with a thread a row), and the two tokens of a pair, adjacent in the fragment, go
-// through each float operation together (.f32x2: each half rounded on its own, as the scalar operation rounds it):
-// half the shared-memory reads of scales and half the float instructions. The arithmetic per (row, token, group) and
-// its order are those of the general epilogue below.
-template <bool TAIL>
-__device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int quarter, int sub, int lane,
+// The epilogue of 64- and 32-token tiles. Epilogue warp w reads TMEM lane quarter w % 4 and token columns
+// (w - 4) / 4 * TPW .. + TPW as 16x256b fragments of both 16-lane halves, so that thread t keeps four rows
+// (quarter * 32 + t/4 + 8i) x PP = BN / 32 token pairs (8p + 2(t%4), +1 of the warp's TPW). Each activation-scale pair
+// a thread reads from shared memory then serves four rows (against one with a thread a row), and the two tokens of a
+// pair, adjacent in the fragment, go through each float operation together (.f32x2: each half rounded on its own, as
+// the scalar operation rounds it): half the shared-memory reads of scales and half the float instructions. The
+// arithmetic per (row, token, group) and its order are those of the general epilogue below.
+template <int BN, bool TAIL>
+__device__ __forceinline__ void epilogue_4x4(Smem<BN> &s, uint32_t tmem, int quarter, int sub, int lane,
                                              const GemmArgs &args, int tiles, int ntok, int kstages, int ng, int ng4,
                                              float one) {
-  constexpr int BN = 64, STAGES = Tile<BN>::STAGES, SLOTS = Tile<BN>::SLOTS;
+  constexpr int STAGES = Tile<BN>::STAGES, SLOTS = Tile<BN>::SLOTS, TPW = Tile<BN>::TPW, PP = BN / 32;
   const int c = lane & 3, rq = lane >> 2;
-  const uint32_t t_lo = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * 16), t_hi = t_lo + (16u << 16);
+  const uint32_t t_lo = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW), t_hi = t_lo + (16u << 16);
   const uint64_t one2 = pk2(__float_as_uint(one), __float_as_uint(one));
   Ring<STAGES> ring;
   Ring<SLOTS> slots;
   for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int row0 = (tile / ntok) * BM, tok0 = (tile % ntok) * BN;
-    uint64_t acc[4][2][4];  // [row rq + 8i][token pair p][chain lane j]
+    uint64_t acc[4][PP][4];  // [row rq + 8i][token pair p][chain lane j]
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-      for (int p = 0; p < 2; p++)
+      for (int p = 0; p < PP; p++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][p][j] = 0;
     for (int k = 0; k < kstages; k++, ring.next(), slots.next()) {
@@ -272,25 +281,25 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
       mbar_wait(&s.slot_full[slot], slots.phase, args.error, 5);
       tc_fence_after();
       const float *wq = &s.ws[st][quarter * 32 + rq][0];  // row rq + 8i's group j: wq[32 * i + j]
-      const float *xq = s.xs[st] + sub * 16 + 2 * c;      // group j's token pair p: xq[j * BN + 8 * p], two floats
+      const float *xq = s.xs[st] + sub * TPW + 2 * c;      // group j's token pair p: xq[j * BN + 8 * p], two floats
       if (!TAIL || 4 * k + 4 <= ng4) {
         // four whole groups. Step q = 2j + h works on group j's half h (rows rq + 8i, i = 2h, 2h + 1): it waits for
         // its own TMEM load, issues the next step's, then computes, so that each load lands during a step's work.
         // Row rq + 8i, pair p: fragment registers 4p + 2(i & 1), +1.
-        uint32_t v[2][8];
+        uint32_t v[2][4 * PP];
         uint32_t wv[4];
-        uint64_t x2[2];
-        tmem_ld_16x256_x2(t_lo + (uint32_t)(slot * 4 * BN), v[0]);
+        uint64_t x2[PP];
+        tmem_ld_16x256<PP>(t_lo + (uint32_t)(slot * 4 * BN), v[0]);
 #pragma unroll
         for (int q = 0; q < 8; q++) {
           const int j = q >> 1, h = q & 1;
-          tmem_wait_ld(v[q & 1]);
+          tmem_wait_ld<PP>(v[q & 1]);
           if (q < 7)
-            tmem_ld_16x256_x2(((q + 1) & 1 ? t_hi : t_lo) + (uint32_t)((slot * 4 + ((q + 1) >> 1)) * BN),
+            tmem_ld_16x256<PP>(((q + 1) & 1 ? t_hi : t_lo) + (uint32_t)((slot * 4 + ((q + 1) >> 1)) * BN),
                               v[(q + 1) & 1]);
           if (h == 0) {
 #pragma unroll
-            for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+            for (int p = 0; p < PP; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
 #pragma unroll
             for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
           }
@@ -300,7 +309,7 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
           for (int ii = 0; ii < 2; ii++) {
             const int i = 2 * h + ii;
 #pragma unroll
-            for (int p = 0; p < 2; p++) {
+            for (int p = 0; p < PP; p++) {
               const int r = 4 * p + 2 * ii;
               const uint64_t sums = pk2(v[q & 1][r], v[q & 1][r + 1]);
               acc[i][p][j] = fma2(one2, acc[i][p][j], mul2(sums, mul2(pk2(wv[i], wv[i]), x2[p])));
@@ -310,15 +319,15 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
       } else {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          uint32_t v[2][8];  // the two 16-lane halves' fragments
+          uint32_t v[2][4 * PP];  // the two 16-lane halves' fragments
           uint32_t wv[4];
-          uint64_t x2[2];
+          uint64_t x2[PP];
           if (j < groups) {
             const uint32_t col = (uint32_t)((slot * 4 + j) * BN);
-            tmem_ld_16x256_x2(t_lo + col, v[0]);
-            tmem_ld_16x256_x2(t_hi + col, v[1]);
+            tmem_ld_16x256<PP>(t_lo + col, v[0]);
+            tmem_ld_16x256<PP>(t_hi + col, v[1]);
 #pragma unroll
-            for (int p = 0; p < 2; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
+            for (int p = 0; p < PP; p++) x2[p] = *reinterpret_cast<const uint64_t *>(xq + j * BN + 8 * p);
 #pragma unroll
             for (int i = 0; i < 4; i++) wv[i] = __float_as_uint(wq[32 * i + j]);
             tmem_wait_ld();
@@ -328,7 +337,7 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
 #pragma unroll
           for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int p = 0; p < 2; p++) {
+            for (int p = 0; p < PP; p++) {
               float x[2];
 #pragma unroll
               for (int e = 0; e < 2; e++) {
@@ -356,7 +365,7 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
 #pragma unroll
       for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int p = 0; p < 2; p++)
+        for (int p = 0; p < PP; p++)
           acc[i][p][0] = fma2(one2, fma2(one2, fma2(one2, acc[i][p][0], acc[i][p][1]), acc[i][p][2]), acc[i][p][3]);
     }
     // each store writes eight consecutive rows of four tokens (four 32-byte pieces)
@@ -365,10 +374,10 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
       const int r = row0 + quarter * 32 + rq + 8 * i;
       if (r >= args.rows) continue;
 #pragma unroll
-      for (int p = 0; p < 2; p++)
+      for (int p = 0; p < PP; p++)
 #pragma unroll
         for (int e = 0; e < 2; e++) {
-          const int tok = tok0 + sub * 16 + 8 * p + 2 * c + e;
+          const int tok = tok0 + sub * TPW + 8 * p + 2 * c + e;
           if (tok < args.count) {
             const float sum = e ? hi_f(acc[i][p][0]) : lo_f(acc[i][p][0]);
             float *o = args.out + (int64_t)tok * args.out_stride + r;
@@ -380,7 +389,7 @@ __device__ __forceinline__ void epilogue_4x4(Smem<64> &s, uint32_t tmem, int qua
 }
 
 // Warp roles: 0 TMA producer, 1 MMA issue, 2 and 3 idle, 4..19 epilogue. Epilogue warp w reads TMEM lane quarter
-// w % 4 (its 32 rows) and token columns (w - 4) / 4 * TPW .. + TPW (64-token tiles: epilogue_4x4 above), and keeps the
+// w % 4 (its 32 rows) and token columns (w - 4) / 4 * TPW .. + TPW (64- and 32-token tiles: epilogue_4x4 above), and keeps the
 // reference's four chain accumulators of each of its (row, token) in registers: the chains, their sum and the groups
 // past the fours all happen in one thread. Tiles go round the blocks (tile = block, block + grid, ...): consecutive
 // tiles share their weight rows, so blocks that run together read each weight row once from HBM.
@@ -500,8 +509,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_EPILOGUE));
     // ---- epilogue
     const int quarter = warp % 4, sub = (warp - EPI_WARP0) / 4;
-    if constexpr (BN == 64) {
-      epilogue_4x4<TAIL>(s, tmem, quarter, sub, lane, args, tiles, ntok, kstages, ng, ng4, one);
+    if constexpr (BN >= 32) {
+      epilogue_4x4<BN, TAIL>(s, tmem, quarter, sub, lane, args, tiles, ntok, kstages, ng, ng4, one);
     } else {
       const int rl = quarter * 32 + lane;  // the row within the tile
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * TPW);
@@ -673,6 +682,16 @@ int gemm_sms() {
   return sm_counts[device];
 }
 
+// time of a stage (128 K bytes of a tile) by tile width, in hundredths of a microsecond at 1965 MHz: measured on the
+// 8B shapes with one tile per SM (16: the general epilogue; 32 and 64: epilogue_4x4)
+constexpr int TC_STAGE_CUS[3] = {73, 88, 92};
+
+int64_t gemm_tc_cost(int rows, int count, int n, int sms, int bn) {
+  const int64_t tiles = (int64_t)((rows + BM - 1) / BM) * ((count + bn - 1) / bn);
+  const int64_t rounds = (tiles + sms - 1) / sms;  // a block walks ceil(tiles / SMs) tiles
+  return rounds * ((n + KSTAGE - 1) / KSTAGE) * TC_STAGE_CUS[bn == 16 ? 0 : bn == 32 ? 1 : 2];
+}
+
 int choose_gemm_bn(int rows, int count, int sms, int widest) {
   // B200FWD_GEMM_BN=16|32|64 fixes the width (a tuning knob for measurements; within what the token maps allow)
   static const int fixed = [] {
@@ -680,19 +699,15 @@ int choose_gemm_bn(int rows, int count, int sms, int widest) {
     const int b = v ? atoi(v) : 0;
     return b == 16 || b == 32 || b == 64 ? b : 0;
   }();
-  if (fixed && fixed <= widest && (fixed == 16 || fixed <= count)) return fixed;
-  // a stage of a tile costs a fixed part (the pipeline's waits, TMEM and scale loads, the MMA chain) and a part that
-  // grows with its BN columns (every column is computed): measured, about 1100 + 17 BN cycles, so 64 columns' worth
-  // of fixed cost; a block walks ceil(tiles / SMs) tiles
-  const int row_tiles = (rows + BM - 1) / BM;
+  if (fixed && fixed <= widest && (fixed == 16 || fixed / 2 < count)) return fixed;
+  // the width of the least estimated time, up to the first that holds every token in one tile (a wider tile costs
+  // little more a stage than a narrower one: its rows of tokens are computed whether or not they exist)
   int best = 16;
   int64_t best_cost = INT64_MAX;
   for (int bn = 16; bn <= widest; bn *= 2) {
-    if (bn > 16 && bn > count) break;
-    const int64_t tiles = (int64_t)row_tiles * ((count + bn - 1) / bn);
-    const int64_t per_block = (tiles + sms - 1) / sms;
-    const int64_t cost = per_block * (bn + 64);
-    if (cost <= best_cost) {
+    if (bn > 16 && bn / 2 >= count) break;
+    const int64_t cost = gemm_tc_cost(rows, count, KSTAGE, sms, bn);
+    if (cost < best_cost) {
       best = bn;
       best_cost = cost;
     }

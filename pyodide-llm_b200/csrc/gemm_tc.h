@@ -41,6 +41,8 @@ int make_token_scale_map(CUtensorMap *map, const float *base, int64_t tokens, in
 int launch_gemm_tc(const GemmMaps &maps, const GemmArgs &args, int bn, cudaStream_t stream);
 // the tile width (16, 32 or 64, at most `widest`) that spreads rows x count best over `sms` SMs
 int choose_gemm_bn(int rows, int count, int sms, int widest);
+// the estimated time of q8_gemm_tc with tiles of bn tokens, in hundredths of a microsecond (measured stage times)
+int64_t gemm_tc_cost(int rows, int count, int n, int sms, int bn);
 // the current device's SM count (after its opt-in)
 int gemm_sms();
 // the kernels' shared-memory opt-in on the current device (before any graph capture)
@@ -56,8 +58,9 @@ int make_lane_weight_maps(CUtensorMap *wmap, CUtensorMap *smap, const void *w, c
 int make_lane_token_maps(CUtensorMap *xmap, CUtensorMap *xsmap, const int8_t *xq, const float *xs, int64_t tokens,
                          int64_t row_bytes, int64_t k, int64_t tp, int bn);
 bool gemm_lanes_fits(int n, int rows, int count);
-// whether the lane split is the faster kernel for rows x count on `sms` SMs (few row tiles)
-bool gemm_lanes_pays(int rows, int count, int sms);
+// whether the lane split is estimated faster than q8_gemm_tc (at its best width up to `widest`) for rows x n by count
+// tokens on `sms` SMs (few row tiles)
+bool gemm_lanes_pays(int rows, int count, int n, int sms, int widest);
 // the tile width for count tokens: one tile up to 64 tokens, else tiles of 64; at most `widest` (16, 32 or 64: the
 // token maps' boxes must fit their tensors)
 int choose_lanes_bn(int count, int widest);

@@ -171,6 +171,23 @@ __device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
                : "r"(taddr));
 }
 
+// 16 TMEM lanes x 8PP columns (PP 256-bit repetitions) from lane taddr.lane, not waited for: thread t holds lane t/4
+// in r[4p], r[4p + 1] (columns 8p + 2(t%4), +1) and lane t/4 + 8 in r[4p + 2], r[4p + 3] (the same columns)
+template <int PP>
+__device__ __forceinline__ void tmem_ld_16x256(uint32_t taddr, uint32_t (&r)[4 * PP]);
+template <>
+__device__ __forceinline__ void tmem_ld_16x256<2>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <>
+__device__ __forceinline__ void tmem_ld_16x256<1>(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
 // a position in a ring of N buffers and the parity of its current round (advanced by one at a time: no division)
 template <int N>
 struct Ring {

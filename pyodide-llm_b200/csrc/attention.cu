@@ -404,6 +404,168 @@ __global__ void attn_values_tiled(float *out, int64_t out_stride, const void *vc
   }
 }
 
+// ---- prompt blocks, register-blocked (heads of a multiple of 64 values, 16-byte rows). The block stages its rows
+// once and each thread keeps a 4 x 4 tile of outputs in registers: every 16-byte shared-memory read then serves four
+// outputs' sums (one with a thread an output), the limit of the kernels above. The arithmetic of each output and its
+// order are those of attn_scores_tiled and attn_values_tiled.
+constexpr int RB_POS = 64;  // positions of a scores block and of a values chunk
+constexpr int RB_VAL = 64;  // values of a head a values block takes
+
+// grid (chunks of RB_POS positions, kv heads, tiles), 64G threads: thread (ty, tx) takes rows 4ty .. 4ty + 3 of the
+// tile (row r: token r / G, head r % G of the kv head) and positions tx, tx + 16, tx + 32, tx + 48 of the chunk; per
+// output the four lane accumulators over the head's dims (lane k takes the dims 4i + k), paired (0, 1) and (2, 3),
+// then (l0+l2)+(l1+l3) times 1/sqrt(hs). q rows start on 16 bytes (q_stride a multiple of 4).
+template <bool HALF, int G>
+__global__ void __launch_bounds__(64 * G, G <= 4 ? 2 : 1)
+    attn_scores_rb(const float *q, int64_t q_stride, const void *kc, float *att, const int32_t *seq,
+                   const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
+                   int hs, int h0, int h1, float one) {
+  pdl_begin();
+  extern __shared__ __align__(16) float sm[];
+  const int kvh = blockIdx.y, chunk = blockIdx.x;
+  const Tile tl = tile_of(tiles, blockIdx.z);
+  const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
+  const int c0 = chunk * RB_POS;
+  if (c0 > last) return;
+  const int rows = min(RB_POS, last + 1 - c0);
+  const int kvDim = nkv * hs, pitch = hs + 4;  // rows 16 bytes apart in the banks
+  float *ks = sm;                             // [RB_POS][pitch]
+  float *qs = sm + RB_POS * pitch;            // [ATT_TT * G][pitch]
+  const int64_t sq = seq ? seq[tl.first] : 0;
+  stage_rows<HALF>(ks, pitch, kc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs, kvDim, hs, rows, true);
+  // the tile's tokens' G heads of this kv head: each token's G * hs floats are contiguous
+  const int h4 = hs / 4;
+  for (int idx = threadIdx.x; idx < tl.count * G * h4; idx += blockDim.x) {
+    const int r = idx / h4, d4 = idx % h4;
+    const float4 v = *reinterpret_cast<const float4 *>(q + (int64_t)(tl.first + r / G) * q_stride +
+                                                      (int64_t)(kvh * G + r % G) * hs + 4 * d4);
+    *reinterpret_cast<float4 *>(qs + r * pitch + 4 * d4) = v;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, tx = lane & 15, ty = (threadIdx.x >> 5) * 2 + (lane >> 4);
+  const float *qrow = qs + 4 * ty * pitch, *krow = ks + tx * pitch;
+  const uint64_t one2 = pk(one, one);
+  uint64_t a01[4][4], a23[4][4];  // [row][position]: lanes 0, 1 and 2, 3
+#pragma unroll
+  for (int e = 0; e < 4; e++)
+#pragma unroll
+    for (int f = 0; f < 4; f++) a01[e][f] = a23[e][f] = 0;
+  for (int d = 0; d < hs; d += 4) {
+    ulonglong2 qv[4], kv[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) qv[e] = *reinterpret_cast<const ulonglong2 *>(qrow + e * pitch + d);
+#pragma unroll
+    for (int f = 0; f < 4; f++) kv[f] = *reinterpret_cast<const ulonglong2 *>(krow + 16 * f * pitch + d);
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+#pragma unroll
+      for (int f = 0; f < 4; f++) {
+        a01[e][f] = fma2(one2, a01[e][f], mul2(qv[e].x, kv[f].x));
+        a23[e][f] = fma2(one2, a23[e][f], mul2(qv[e].y, kv[f].y));
+      }
+  }
+  const float isq = fdiv(1.0f, __fsqrt_rn((float)hs));
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int r = 4 * ty + e, i = r / G, h = kvh * G + r % G;
+    if (i >= tl.count || h < h0 || h >= h1) continue;
+    const int tok = tl.first + i, ptok = pos_of(pos, pos0, tok);
+    float *dst = att + ((int64_t)tok * nh + h) * P;
+#pragma unroll
+    for (int f = 0; f < 4; f++) {
+      const int p = c0 + tx + 16 * f;
+      if (p > ptok) continue;  // causal: a token reads the positions up to its own
+      const float s4 = fadd(fadd(lo(a01[e][f]), lo(a23[e][f])), fadd(hi(a01[e][f]), hi(a23[e][f])));
+      dst[p] = fmul(s4, isq);
+    }
+  }
+}
+
+// grid (kv heads, tiles, hs / RB_VAL), 64G threads: thread (ty, tx) takes rows 4ty .. 4ty + 3 of the tile and the
+// values z * RB_VAL + 4tx .. + 3 of their heads, summed as attn_values_tiled sums them (the positions in fours,
+// ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) then added, on the values in pairs; the positions past the fours one by one).
+// The chunk's values and the tile's weights come to shared memory chunk by chunk. out rows start on 16 bytes.
+template <bool HALF, int G>
+__global__ void __launch_bounds__(64 * G)
+    attn_values_rb(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
+                   const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
+                   int hs, int h0, int h1, float one) {
+  pdl_begin();
+  extern __shared__ __align__(16) float sm[];
+  constexpr int ROWS = ATT_TT * G, VP = RB_VAL + 4, WP = RB_POS + 4;
+  const int kvh = blockIdx.x, v0 = blockIdx.z * RB_VAL;
+  const Tile tl = tile_of(tiles, blockIdx.y);
+  const int kvDim = nkv * hs;
+  float *vs = sm;                  // [RB_POS][VP]: the chunk's positions' values v0 .. v0 + RB_VAL
+  float *wsm = sm + RB_POS * VP;   // [ROWS][WP]: the rows' weights of the chunk's positions (0 past a token's own)
+  const int lane = threadIdx.x & 31, tx = lane & 15, ty = (threadIdx.x >> 5) * 2 + (lane >> 4);
+  const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
+  const int64_t sq = seq ? seq[tl.first] : 0;
+  int count[4];  // positions of row 4ty + e's token (0: no such row)
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int r = 4 * ty + e, h = kvh * G + r % G;
+    count[e] = r / G < tl.count && h >= h0 && h < h1 ? pos_of(pos, pos0, tl.first + r / G) + 1 : 0;
+  }
+  const uint64_t one2 = pk(one, one);
+  uint64_t o[4][2];  // [row][value pair]: values 4tx, +1 and 4tx + 2, +3
+#pragma unroll
+  for (int e = 0; e < 4; e++) o[e][0] = o[e][1] = 0;
+  for (int c0 = 0; c0 <= last; c0 += RB_POS) {
+    const int rows = min(RB_POS, last + 1 - c0);
+    __syncthreads();  // the previous chunk is done with
+    stage_rows<HALF>(vs, VP, vc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs + v0, kvDim, RB_VAL, rows,
+                     true);
+    for (int idx = threadIdx.x; idx < ROWS * RB_POS; idx += blockDim.x) {
+      const int r = idx / RB_POS, p = idx % RB_POS, i = r / G, hh = kvh * G + r % G;
+      float w = 0.0f;
+      if (i < tl.count && p < rows && hh >= h0 && hh < h1 && c0 + p <= pos_of(pos, pos0, tl.first + i))
+        w = att[((int64_t)(tl.first + i) * nh + hh) * P + c0 + p];
+      wsm[r * WP + p] = w;
+    }
+    __syncthreads();
+    for (int p = 0; p < rows; p += 4) {
+      const int P0 = c0 + p;
+      float4 vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) vv[u] = *reinterpret_cast<const float4 *>(vs + (p + u) * VP + 4 * tx);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float4 w = *reinterpret_cast<const float4 *>(wsm + (4 * ty + e) * WP + p);
+        if (P0 + 4 <= (count[e] & ~3)) {
+          // ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) for both values of each pair at once, then added to the sums
+          const uint64_t w0 = pk(w.x, w.x), w1 = pk(w.y, w.y), w2 = pk(w.z, w.z), w3 = pk(w.w, w.w);
+          const uint64_t s01a = fma2(one2, mul2(w0, pk(vv[0].x, vv[0].y)), mul2(w1, pk(vv[1].x, vv[1].y)));
+          const uint64_t s23a = fma2(one2, mul2(w2, pk(vv[2].x, vv[2].y)), mul2(w3, pk(vv[3].x, vv[3].y)));
+          o[e][0] = fma2(one2, o[e][0], fma2(one2, s01a, s23a));
+          const uint64_t s01b = fma2(one2, mul2(w0, pk(vv[0].z, vv[0].w)), mul2(w1, pk(vv[1].z, vv[1].w)));
+          const uint64_t s23b = fma2(one2, mul2(w2, pk(vv[2].z, vv[2].w)), mul2(w3, pk(vv[3].z, vv[3].w)));
+          o[e][1] = fma2(one2, o[e][1], fma2(one2, s01b, s23b));
+        } else if (P0 < count[e]) {
+          // the positions past the fours, one at a time (kernel.ts:548-564)
+          const float wu[4] = {w.x, w.y, w.z, w.w};
+          float a[4] = {lo(o[e][0]), hi(o[e][0]), lo(o[e][1]), hi(o[e][1])};
+          for (int u = 0; u < 4 && P0 + u < count[e]; u++) {
+            a[0] = fadd(a[0], fmul(wu[u], vv[u].x));
+            a[1] = fadd(a[1], fmul(wu[u], vv[u].y));
+            a[2] = fadd(a[2], fmul(wu[u], vv[u].z));
+            a[3] = fadd(a[3], fmul(wu[u], vv[u].w));
+          }
+          o[e][0] = pk(a[0], a[1]);
+          o[e][1] = pk(a[2], a[3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    if (!count[e]) continue;
+    const int r = 4 * ty + e, h = kvh * G + r % G;
+    float *dst = out + (int64_t)(tl.first + r / G) * out_stride + (int64_t)h * hs + v0 + 4 * tx;
+    *reinterpret_cast<float4 *>(dst) = make_float4(lo(o[e][0]), hi(o[e][0]), lo(o[e][1]), hi(o[e][1]));
+  }
+}
+
 // ---- single query tokens (decode): no tile shares the keys and values, so each thread loads its own straight from
 // the cache (16-byte loads of its position's row for the scores; a pair of values per position for the weighted
 // sum), with no shared-memory staging and no block-wide waits in the loops.
@@ -800,6 +962,26 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     return 0;
   }
   const int chunks = (max_count + ATT_CH - 1) / ATT_CH;
+  if (tiles && vec && hs % RB_VAL == 0 && q_stride % 4 == 0 && out_stride % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    // prompt blocks: the register-blocked kernels
+    const size_t smem_s = (size_t)(RB_POS + ATT_TT * G) * (hs + 4) * sizeof(float);
+    const size_t smem_v = (size_t)(RB_POS * (RB_VAL + 4) + ATT_TT * G * (RB_POS + 4)) * sizeof(float);
+    if (smem_s <= MAX_TILE_SMEM && smem_v <= MAX_TILE_SMEM) {
+      B200_CUDA(cudaFuncSetAttribute(attn_scores_rb<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)MAX_TILE_SMEM));
+      B200_CUDA(cudaFuncSetAttribute(attn_values_rb<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)MAX_TILE_SMEM));
+      launch(attn_scores_rb<HALF, G>, dim3((max_count + RB_POS - 1) / RB_POS, nkv, ntiles), 64 * G, smem_s, stream, q,
+             q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
+      B200_LAUNCHED("attn_scores_rb");
+      CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
+      launch(attn_values_rb<HALF, G>, dim3(nkv, ntiles, hs / RB_VAL), 64 * G, smem_v, stream, out, out_stride, vc,
+             att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
+      B200_LAUNCHED("attn_values_rb");
+      return 0;
+    }
+  }
   const int tt = tiles ? ATT_TT : 1;
   const int hsp = (hs + 3) & ~3;
   const size_t smem_scores = (size_t)(ATT_CH * (hsp + 4) + tt * G * hsp) * sizeof(float);

@@ -329,3 +329,42 @@ def test_generate_many_slots_are_independent():
                                   1.1, [p for p in prompts], [len(p) for p in prompts], randoms, [])
     for i in range(3):
         assert list(ids[i][:made[i]]) == alone[i], i
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(4, 4), (4, 2), (8, 2), (8, 1)])
+@pytest.mark.parametrize("half_keys", [True, False])
+def test_prompt_blocks_of_wide_heads(heads, kv_heads, half_keys):
+    """Prompt blocks of heads of 64 values (the register-blocked prompt attention: 1, 2, 4 and 8 query heads per kv
+    head): three sequences' prompts of ragged lengths, run in two calls of several sequences each, so that tiles of
+    up to 16 tokens read keys and values past three 64-position chunks and the last tile of a run is short; each
+    sequence's last logits against the oracle's token-by-token forward, to the bit."""
+    dim = 64 * heads
+    header = (dim, 2 * dim, 1, heads, kv_heads, 320, 512)
+    data = ck.synthetic_checkpoint(header, seed=heads * 10 + kv_heads, norm="normal")
+    plan = ck.make_plan(header, lambda o, n: data[o:o + n])
+    lengths = [150, 83, 211]
+    rng = np.random.default_rng(heads + kv_heads)
+    prompts = [rng.integers(0, 320, n).astype(np.int32) for n in lengths]
+    eng = Engine(data, plan, half_keys=half_keys, slots=3, max_tokens=512, capacity=256)
+    got = {}
+    for lo, hi in ((0, 100), (100, 256)):
+        slots, tokens, pos, want = [], [], [], []
+        for s, p in enumerate(prompts):
+            n = min(hi, len(p)) - lo
+            if n <= 0:
+                continue
+            slots += [s] * n
+            tokens += list(p[lo:lo + n])
+            pos += list(range(lo, lo + n))
+            want += [lo + i == len(p) - 1 for i in range(n)]
+        logits, _ = eng.run(np.array(slots), np.array(tokens), np.array(pos), want=np.array(want))
+        ends = [s for s, w in zip(slots, want) if w]
+        for s, row in zip(ends, logits):
+            got[s] = row.copy()
+    eng.release()
+    for s, p in enumerate(prompts):
+        ref = oracle.OracleEngine(data, plan, half_keys=1 if half_keys else 0, threads=2)
+        ref.forward_many([int(t) for t in p[:-1]], 0)
+        want = ref.forward(int(p[-1]), len(p) - 1)
+        ref.close()
+        assert np.array_equal(bits(got[s]), bits(want)), s

@@ -484,9 +484,10 @@ __global__ void __launch_bounds__(64 * G, G <= 4 ? 2 : 1)
 // grid (kv heads, tiles, hs / RB_VAL), 64G threads: thread (ty, tx) takes rows 4ty .. 4ty + 3 of the tile and the
 // values z * RB_VAL + 4tx .. + 3 of their heads, summed as attn_values_tiled sums them (the positions in fours,
 // ((w0 v0 + w1 v1) + (w2 v2 + w3 v3)) then added, on the values in pairs; the positions past the fours one by one).
-// The chunk's values and the tile's weights come to shared memory chunk by chunk. out rows start on 16 bytes.
+// The chunk's values and the tile's weights come to shared memory chunk by chunk, each loaded into registers while
+// the chunk before is summed. out rows start on 16 bytes; att rows too (P a multiple of four).
 template <bool HALF, int G>
-__global__ void __launch_bounds__(64 * G)
+__global__ void __launch_bounds__(64 * G, G <= 4 ? 3 : 1)
     attn_values_rb(float *out, int64_t out_stride, const void *vc, const float *att, const int32_t *seq,
                    const int32_t *pos, int pos0, const int32_t *tiles, int64_t seq_stride, int P, int nh, int nkv,
                    int hs, int h0, int h1, float one) {
@@ -501,29 +502,82 @@ __global__ void __launch_bounds__(64 * G)
   const int lane = threadIdx.x & 31, tx = lane & 15, ty = (threadIdx.x >> 5) * 2 + (lane >> 4);
   const int last = pos_of(pos, pos0, tl.first + tl.count - 1);
   const int64_t sq = seq ? seq[tl.first] : 0;
-  int count[4];  // positions of row 4ty + e's token (0: no such row)
-#pragma unroll
-  for (int e = 0; e < 4; e++) {
-    const int r = 4 * ty + e, h = kvh * G + r % G;
-    count[e] = r / G < tl.count && h >= h0 && h < h1 ? pos_of(pos, pos0, tl.first + r / G) + 1 : 0;
+  // each row's positions (its token's own + 1; 0: no such row), then the chunks: chunk c + 1's values and weights
+  // are loaded into registers while chunk c is summed, and stored to shared memory after it
+  constexpr int ES = HALF ? 2 : 4, PR = RB_VAL * ES / 16;          // 16-byte pieces of a position's values
+  constexpr int NV = (RB_POS * PR + 64 * G - 1) / (64 * G), NW = 4;  // pieces and weight fours a thread moves
+  __shared__ int rcount[ROWS];
+  for (int r = threadIdx.x; r < ROWS; r += blockDim.x) {
+    const int i = r / G, h = kvh * G + r % G;
+    rcount[r] = i < tl.count && h >= h0 && h < h1 ? pos_of(pos, pos0, tl.first + i) + 1 : 0;
   }
+  __syncthreads();
+  int count[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) count[e] = rcount[4 * ty + e];
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(vc) + (sq * seq_stride + (int64_t)kvh * hs + v0) * ES;
+  uint4 vreg[NV];
+  float4 wreg[NW];
+  auto fetch = [&](int c0) {
+    const int rows = min(RB_POS, last + 1 - c0);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int idx = threadIdx.x + k * 64 * G, r = idx / PR;
+      vreg[k] = make_uint4(0, 0, 0, 0);
+      if (idx < RB_POS * PR && r < rows)
+        vreg[k] = *reinterpret_cast<const uint4 *>(vbase + (int64_t)(c0 + r) * kvDim * ES + (idx % PR) * 16);
+    }
+#pragma unroll
+    for (int k = 0; k < NW; k++) {
+      const int idx = threadIdx.x + k * 64 * G, r = idx / (RB_POS / 4), p = c0 + 4 * (idx % (RB_POS / 4));
+      const int cnt = rcount[r];
+      float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (p < cnt) {  // P a multiple of four: the whole four lies in the row
+        w = *reinterpret_cast<const float4 *>(att + ((int64_t)(tl.first + r / G) * nh + kvh * G + r % G) * P + p);
+        if (p + 1 >= cnt) w.y = 0.f;
+        if (p + 2 >= cnt) w.z = 0.f;
+        if (p + 3 >= cnt) w.w = 0.f;
+      }
+      wreg[k] = w;
+    }
+  };
+  auto store = [&]() {
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const int idx = threadIdx.x + k * 64 * G, r = idx / PR, piece = idx % PR;
+      if (idx >= RB_POS * PR) continue;
+      float *d = vs + r * VP + piece * (16 / ES);
+      if (HALF) {
+        const uint32_t w[4] = {vreg[k].x, vreg[k].y, vreg[k].z, vreg[k].w};
+        float f[8];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          f[2 * u] = half_to_float((uint16_t)(w[u] & 0xffff));
+          f[2 * u + 1] = half_to_float((uint16_t)(w[u] >> 16));
+        }
+        *reinterpret_cast<float4 *>(d) = make_float4(f[0], f[1], f[2], f[3]);
+        *reinterpret_cast<float4 *>(d + 4) = make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+        *reinterpret_cast<uint4 *>(d) = vreg[k];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NW; k++) {
+      const int idx = threadIdx.x + k * 64 * G;
+      *reinterpret_cast<float4 *>(wsm + (idx / (RB_POS / 4)) * WP + 4 * (idx % (RB_POS / 4))) = wreg[k];
+    }
+  };
   const uint64_t one2 = pk(one, one);
   uint64_t o[4][2];  // [row][value pair]: values 4tx, +1 and 4tx + 2, +3
 #pragma unroll
   for (int e = 0; e < 4; e++) o[e][0] = o[e][1] = 0;
+  fetch(0);
   for (int c0 = 0; c0 <= last; c0 += RB_POS) {
     const int rows = min(RB_POS, last + 1 - c0);
     __syncthreads();  // the previous chunk is done with
-    stage_rows<HALF>(vs, VP, vc, sq * seq_stride + (int64_t)c0 * kvDim + (int64_t)kvh * hs + v0, kvDim, RB_VAL, rows,
-                     true);
-    for (int idx = threadIdx.x; idx < ROWS * RB_POS; idx += blockDim.x) {
-      const int r = idx / RB_POS, p = idx % RB_POS, i = r / G, hh = kvh * G + r % G;
-      float w = 0.0f;
-      if (i < tl.count && p < rows && hh >= h0 && hh < h1 && c0 + p <= pos_of(pos, pos0, tl.first + i))
-        w = att[((int64_t)(tl.first + i) * nh + hh) * P + c0 + p];
-      wsm[r * WP + p] = w;
-    }
+    store();
     __syncthreads();
+    if (c0 + RB_POS <= last) fetch(c0 + RB_POS);
     for (int p = 0; p < rows; p += 4) {
       const int P0 = c0 + p;
       float4 vv[4];
@@ -962,8 +1016,9 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     return 0;
   }
   const int chunks = (max_count + ATT_CH - 1) / ATT_CH;
-  if (tiles && vec && hs % RB_VAL == 0 && q_stride % 4 == 0 && out_stride % 4 == 0 &&
-      reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+  if (tiles && vec && hs % RB_VAL == 0 && q_stride % 4 == 0 && out_stride % 4 == 0 && P % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(att) % 16 == 0) {
     // prompt blocks: the register-blocked kernels
     const size_t smem_s = (size_t)(RB_POS + ATT_TT * G) * (hs + 4) * sizeof(float);
     const size_t smem_v = (size_t)(RB_POS * (RB_VAL + 4) + ATT_TT * G * (RB_POS + 4)) * sizeof(float);

@@ -256,8 +256,9 @@ def reference_arm(args):
 
 # measured DRAM bytes / algorithmic bytes of the decode-shape matmul launches (ncu, one launch each): q8_gemm_tc at
 # 28672 x 4096 136.25 / 139.76 MB, q8_gemm_lanes at 4096 x 14336 67.91 / 68.14 MB; weighted by the bytes each kernel
-# moves in a decode pass (q|k|v, w1|w3 and the classifier on the first, o and w2 on the second: 5724 and 2720 MB)
-TRAFFIC_RATIO = (5724 * (136.25 / 139.76) + 2720 * (67.91 / 68.14)) / (5724 + 2720)
+# moves in a decode pass at 64 tokens (w1|w3 and the classifier on the first, q|k|v, o and w2 on the second: 5096 and
+# 3793 MB)
+TRAFFIC_RATIO = (5096 * (136.25 / 139.76) + 3793 * (67.91 / 68.14)) / (5096 + 3793)
 
 
 def matmul_roofline(eng, M, peaks, reps=3):

@@ -952,8 +952,8 @@ int launch_softmax(float *att, const int32_t *pos, int pos0, int P, int nh, int 
                    size_t smem_soft, cudaStream_t stream) {
   if (max_count <= SOFTMAX_ROW_MAX) {
     const int64_t rows = (int64_t)count * nh;
-    launch(attn_softmax_rows, (unsigned)((rows + SOFTMAX_ROWS - 1) / SOFTMAX_ROWS), 32 * SOFTMAX_ROWS, 0, stream,
-        att, pos, pos0, P, nh, h0, h1, count);
+    launch(attn_softmax_rows, (unsigned)((rows + SOFTMAX_ROWS - 1) / SOFTMAX_ROWS), 32 * SOFTMAX_ROWS, 0, stream, att,
+           pos, pos0, P, nh, h0, h1, count);
     B200_LAUNCHED("attn_softmax_rows");
     return 0;
   }
@@ -976,8 +976,7 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     B200_CUDA(cudaFuncSetAttribute(attn_scores_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));
     launch(attn_scores_decode<HALF, G>, dim3((max_count + DEC_POS - 1) / DEC_POS, nkv, count), DEC_POS, smem_scores,
-                                  stream, q, q_stride, kc, att, seq, pos, pos0,
-                                                                            seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
+           stream, q, q_stride, kc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
     B200_LAUNCHED("attn_scores_decode");
     CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
     // the head's values split over `parts` blocks per token (more blocks streaming at once; the positions stay in
@@ -990,9 +989,8 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
       return c == 1 || c == 2 || c == 4 || c == 8 ? c : 2;
     }();
     if (HALF && hs % 64 == 0) {
-      launch(attn_values_decode_h<G>, dim3(nkv * (hs / 64), count), 32, 0, stream,
-          out, out_stride, static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
-          1.0f);
+      launch(attn_values_decode_h<G>, dim3(nkv * (hs / 64), count), 32, 0, stream, out, out_stride,
+             static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
       B200_LAUNCHED("attn_values_decode_h");
       return 0;
     }
@@ -1009,9 +1007,9 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
     if (smem_values > MAX_TILE_SMEM) return fail(B200FWD_EUNSUPPORTED, "attention: heads too wide for a value chunk");
     B200_CUDA(cudaFuncSetAttribute(attn_values_decode<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)MAX_TILE_SMEM));
-    launch(attn_values_decode<HALF, G>, dim3(nkv, count, parts), threads, smem_values, stream,
-        out, out_stride, vc, att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
-        P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0, 1.0f);
+    launch(attn_values_decode<HALF, G>, dim3(nkv, count, parts), threads, smem_values, stream, out, out_stride, vc, att,
+           seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1,
+           P % 4 == 0 && reinterpret_cast<uintptr_t>(att) % 16 == 0 ? 1 : 0, 1.0f);
     B200_LAUNCHED("attn_values_decode");
     return 0;
   }
@@ -1031,8 +1029,8 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
              q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
       B200_LAUNCHED("attn_scores_rb");
       CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
-      launch(attn_values_rb<HALF, G>, dim3(nkv, ntiles, hs / RB_VAL), 64 * G, smem_v, stream, out, out_stride, vc,
-             att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
+      launch(attn_values_rb<HALF, G>, dim3(nkv, ntiles, hs / RB_VAL), 64 * G, smem_v, stream, out, out_stride, vc, att,
+             seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
       B200_LAUNCHED("attn_values_rb");
       return 0;
     }
@@ -1047,13 +1045,13 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
                                  (int)MAX_TILE_SMEM));
   B200_CUDA(cudaFuncSetAttribute(attn_values_tiled<HALF, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)MAX_TILE_SMEM));
-  launch(attn_scores_tiled<HALF, G>, dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream,
-      q, q_stride, kc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
+  launch(attn_scores_tiled<HALF, G>, dim3(chunks, nkv, ntiles), ATT_CH, smem_scores, stream, q, q_stride, kc, att, seq,
+         pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_scores_tiled");
   CHECK_ATT(launch_softmax(att, pos, pos0, P, nh, h0, h1, count, max_count, smem_soft, stream));
   const int threads = ((G * ((hs + 1) / 2) + 31) / 32) * 32;
-  launch(attn_values_tiled<HALF, G>, dim3(nkv, ntiles), threads, smem_values, stream,
-      out, out_stride, vc, att, seq, pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
+  launch(attn_values_tiled<HALF, G>, dim3(nkv, ntiles), threads, smem_values, stream, out, out_stride, vc, att, seq,
+         pos, pos0, tiles, seq_stride, P, nh, nkv, hs, h0, h1, vec, 1.0f);
   B200_LAUNCHED("attn_values_tiled");
   return 0;
 }

@@ -119,7 +119,8 @@ int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_
     a.out_stride = out_stride;
     a.accumulate = 0;
     GemmMaps maps;
-    if (!rc && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) && gemm_lanes_pays(rows, count, n, sms, widest)) {
+    if (!rc && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) &&
+        gemm_lanes_pays(rows, count, n, sms, widest)) {
       // n a multiple of 128 and few row tiles: the lane-split kernel (a cluster of four CTAs per tile)
       const int lbn = choose_lanes_bn(count, widest);
       rc = make_lane_weight_maps(&maps.w, &maps.ws, wq, ws, n, rows, ws_stride);

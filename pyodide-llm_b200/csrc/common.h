@@ -52,7 +52,9 @@ inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 #ifdef __CUDACC__
 // the next kernel in the stream may be scheduled once every block of this one has started
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 // until the kernel before this one in the stream has completed and its writes are visible
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // the first statement of every kernel launched by launch(): nothing before it reads or writes global memory

@@ -318,6 +318,79 @@ __global__ void swiglu_quantize_kernel(const float *h1, const float *h3, int64_t
                  xs + (int64_t)tok * s_stride + (int64_t)g * g_stride, shift);
 }
 
+// quantize_x of a group of 32 values held four a lane by eight consecutive lanes (lane l % 8 holding values
+// 4(l % 8) .. + 3): each of a lane's four values is one of quantize_x's lane classes (index mod 4), so each class's
+// largest |value| is a max over the eight lanes (kernel.ts:129-156 groupMax); then the same scalar comparisons,
+// scale and rounding as quantize_group. Every lane of the warp calls it (the shuffles); live lanes store their four
+// bytes at xq (4-byte aligned) and the group's first lane the scale at *xs.
+__device__ __forceinline__ void quantize_four(const float (&o)[4], bool live, int lane, int bias, int shift,
+                                              int8_t *xq, float *xs) {
+  float m[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    m[c] = fabsf(o[c]);
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 1));
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 2));
+    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 4));
+  }
+  if (!live) return;
+  float amax = m[0];
+  if (m[1] > amax) amax = m[1];
+  if (m[2] > amax) amax = m[2];
+  if (m[3] > amax) amax = m[3];
+  const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
+  const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int c = 0; c < 4; c++) packed |= (uint32_t)(uint8_t)(int8_t)(quantize_one(o[c], inv, bias) - shift) << (8 * c);
+  *reinterpret_cast<uint32_t *>(xq) = packed;
+  if ((lane & 7) == 0) *xs = scale;
+}
+
+// rmsnorm + quantize_x with four consecutive values a thread (16-byte loads): the norm's scale as
+// norm_quantize_kernel computes it, then each thread's values w * (s * x) (and the outlier columns taken out as it
+// takes them) quantized by quantize_four, a group on eight lanes, so that a block of 1024 threads quantizes 128
+// groups in one pass. One block per token; x rows and w 16-byte aligned, xq rows 4-byte aligned.
+__global__ void norm_quantize_v4_kernel(const float *x, int64_t x_stride, const float *w, int n, float eps, int bias,
+                                        int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride, int64_t g_stride,
+                                        const int32_t *channels, int nch, float *picked, float *out_f,
+                                        int64_t out_stride, int shift) {
+  pdl_begin();
+  __shared__ float part[5];
+  extern __shared__ float sq[];
+  const int tok = blockIdx.x, lane = threadIdx.x & 31, n4 = n >> 2;
+  const float *xr = x + (int64_t)tok * x_stride;
+  // the first pass's values and weights, read before the norm's serial chain (they do not depend on it)
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const bool live0 = (int)threadIdx.x < n4;
+  const float4 x0 = live0 ? reinterpret_cast<const float4 *>(xr)[threadIdx.x] : zero;
+  const float4 w0 = live0 ? reinterpret_cast<const float4 *>(w)[threadIdx.x] : zero;
+  const float s = norm_scale(xr, n, eps, sq, part);
+  for (int base = 0; base < n4; base += blockDim.x) {
+    const int j4 = base + threadIdx.x;
+    const bool live = j4 < n4;
+    const float4 xv = base == 0 ? x0 : live ? reinterpret_cast<const float4 *>(xr)[j4] : zero;
+    const float4 wv = base == 0 ? w0 : live ? reinterpret_cast<const float4 *>(w)[j4] : zero;
+    const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    float o[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int j = 4 * j4 + c;
+      float v = fmul(wa[c], fmul(s, xa[c]));
+      if (live && out_f) out_f[(int64_t)tok * out_stride + j] = v;
+      for (int k = 0; k < nch; k++) {
+        if (live && channels[k] == j) {
+          picked[(int64_t)tok * nch + k] = v;
+          v = 0.0f;
+        }
+      }
+      o[c] = v;
+    }
+    quantize_four(o, live, lane, bias, shift, xq + (int64_t)tok * q_stride + 4 * j4,
+                  xs + (int64_t)tok * s_stride + (int64_t)(j4 >> 3) * g_stride);
+  }
+}
+
 // quantize_kernel (SWIGLU false: x = h1) and swiglu_quantize_kernel (true) with four consecutive values a thread
 // (16-byte loads): eight lanes a group, four groups a warp. A thread's four values are one of each of quantize_x's
 // lane classes (index mod 4), so each class's largest |value| is a max over the group's eight lanes; then the same
@@ -350,27 +423,8 @@ __global__ void quantize_v4_kernel(const float *h1, const float *h3, int64_t str
       for (int c = 0; c < 4; c++) o[c] = va[c];
     }
   }
-  // groupMax's lane-class maxima (kernel.ts:129-156): class c over the group's eight lanes
-  float m[4];
-#pragma unroll
-  for (int c = 0; c < 4; c++) {
-    m[c] = fabsf(o[c]);
-    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 1));
-    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 2));
-    m[c] = wmax(m[c], __shfl_xor_sync(FULL, m[c], 4));
-  }
-  if (!live) return;
-  float amax = m[0];
-  if (m[1] > amax) amax = m[1];
-  if (m[2] > amax) amax = m[2];
-  if (m[3] > amax) amax = m[3];
-  const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
-  const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
-  uint32_t packed = 0;
-#pragma unroll
-  for (int c = 0; c < 4; c++) packed |= (uint32_t)(uint8_t)(int8_t)(quantize_one(o[c], inv, bias) - shift) << (8 * c);
-  *reinterpret_cast<uint32_t *>(xq + (int64_t)tok * q_stride + j) = packed;
-  if (sub == 0) xs[(int64_t)tok * s_stride + (int64_t)g * g_stride] = scale;
+  quantize_four(o, live, lane, bias, shift, xq + (int64_t)tok * q_stride + j,
+                xs + (int64_t)tok * s_stride + (int64_t)g * g_stride);
 }
 
 __global__ void embed_kernel(const int8_t *w, const float *s, int sstride, const int32_t *tokens, int count, int dim,
@@ -592,7 +646,8 @@ int launch_matvec(const MatJobs &jobs, const int8_t *xq, const float *xs, int64_
   if (jobs.n % 32) return fail(B200FWD_EINVAL, "matvec: n must be whole groups of 32");
   const unsigned grid = std::min<unsigned>(blocks_for(jobs.total_rows, MV_WARPS), 148u * 32u);
   const int mt = count >= 8 ? 8 : count >= 4 ? 4 : count >= 2 ? 2 : 1;
-#define B200_MV(MT, R) launch(matvec_kernel<MT, R>, grid, MV_WARPS * 32, 0, stream, jobs, xq, xs, q_stride, s_stride, g_stride, count)
+#define B200_MV(MT, R) \
+  launch(matvec_kernel<MT, R>, grid, MV_WARPS * 32, 0, stream, jobs, xq, xs, q_stride, s_stride, g_stride, count)
   if (relaxed) {
     switch (mt) {
       case 8: B200_MV(8, true); break;
@@ -623,9 +678,15 @@ int launch_norm_quantize(const float *x, int64_t x_stride, const float *w, int n
   // a block per token: the squares and the groups' quantization spread over the block (only the four lane chains of
   // the norm are serial); 1024 threads while the tokens leave SMs free, 256 (more tokens' chains at once) past that
   const int threads = count <= 148 ? 1024 : 256;
+  if (reinterpret_cast<uintptr_t>(x) % 16 == 0 && x_stride % 4 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(xq) % 4 == 0 && q_stride % 4 == 0) {
+    launch(norm_quantize_v4_kernel, count, threads, (size_t)n * 4, stream, x, x_stride, w, n, eps, bias, xq, q_stride,
+           xs, s_stride, g_stride, channels, nch, picked, out_f, out_stride, shift);
+    B200_LAUNCHED("norm_quantize_v4_kernel");
+    return 0;
+  }
   launch(norm_quantize_kernel, count, threads, (size_t)n * 4, stream, x, x_stride, w, n, eps, bias, xq, q_stride, xs,
-                                                                  s_stride, g_stride, channels, nch, picked, out_f,
-                                                                  out_stride, shift);
+         s_stride, g_stride, channels, nch, picked, out_f, out_stride, shift);
   B200_LAUNCHED("norm_quantize_kernel");
   return 0;
 }
@@ -637,14 +698,13 @@ int launch_quantize(const float *x, int64_t x_stride, int n, int bias, int count
   if (count > 65535) return fail(B200FWD_EINVAL, "quantize_x: more than 65535 tokens");
   if (reinterpret_cast<uintptr_t>(x) % 16 == 0 && x_stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 &&
       q_stride % 4 == 0) {
-    launch(quantize_v4_kernel<false>, dim3(blocks_for(n / 32, 32), count), 256, 0, stream, x, nullptr, x_stride, n, bias,
-                                                                                       xq, q_stride, xs, s_stride,
-                                                                                       g_stride, shift);
+    launch(quantize_v4_kernel<false>, dim3(blocks_for(n / 32, 32), count), 256, 0, stream, x, nullptr, x_stride, n,
+           bias, xq, q_stride, xs, s_stride, g_stride, shift);
     B200_LAUNCHED("quantize_v4_kernel");
     return 0;
   }
   launch(quantize_kernel, dim3(blocks_for(n / 32, 8), count), 256, 0, stream, x, x_stride, n, bias, count, xq, q_stride,
-                                                                          xs, s_stride, g_stride, shift);
+         xs, s_stride, g_stride, shift);
   B200_LAUNCHED("quantize_kernel");
   return 0;
 }
@@ -659,14 +719,12 @@ int launch_swiglu_quantize(const float *h1, const float *h3, int64_t stride, int
                   stride % 4 == 0 && reinterpret_cast<uintptr_t>(xq) % 4 == 0 && q_stride % 4 == 0;
   if (v4) {
     launch(quantize_v4_kernel<true>, dim3(blocks_for(n / 32, 32), count), 256, 0, stream, h1, h3, stride, n, bias, xq,
-                                                                                      q_stride, xs, s_stride,
-                                                                                      g_stride, shift);
+           q_stride, xs, s_stride, g_stride, shift);
     B200_LAUNCHED("quantize_v4_kernel<swiglu>");
     return 0;
   }
   launch(swiglu_quantize_kernel, dim3(blocks_for(n / 32, 8), count), 256, 0, stream, h1, h3, stride, n, bias, count, xq,
-                                                                                 q_stride, xs, s_stride, g_stride,
-                                                                                 shift);
+         q_stride, xs, s_stride, g_stride, shift);
   B200_LAUNCHED("swiglu_quantize_kernel");
   return 0;
 }
@@ -675,7 +733,7 @@ int launch_embed(const int8_t *w, const float *s, int sstride, const int32_t *to
                  int64_t x_stride, cudaStream_t stream) {
   if (count <= 0) return 0;
   launch(embed_kernel, blocks_for((int64_t)count * dim, 256), 256, 0, stream, w, s, sstride, tokens, count, dim, x,
-                                                                          x_stride);
+         x_stride);
   B200_LAUNCHED("embed_kernel");
   return 0;
 }
@@ -688,8 +746,7 @@ int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v
   const int total = (nh + nkv) * (hs / 2) + nkv * hs;
   dim3 grid(blocks_for(total, 256), count);
   launch(rope_cache_kernel, grid, 256, 0, stream, q, q_stride, k, v, kv_stride, cos, sin, pos, seq,
-                                              reinterpret_cast<uint8_t *>(kc), reinterpret_cast<uint8_t *>(vc),
-                                              seq_stride, half, nh, nkv, hs, rot);
+         reinterpret_cast<uint8_t *>(kc), reinterpret_cast<uint8_t *>(vc), seq_stride, half, nh, nkv, hs, rot);
   B200_LAUNCHED("rope_cache_kernel");
   return 0;
 }
@@ -716,7 +773,7 @@ int launch_add_columns(float *y, int64_t y_stride, const float *rows, const floa
                        int n, int count, cudaStream_t stream) {
   if (count <= 0 || nc <= 0) return 0;
   launch(add_columns_kernel, blocks_for((int64_t)n * count, 256), 256, 0, stream, y, y_stride, rows, a, a_stride, nc, n,
-                                                                             count);
+         count);
   B200_LAUNCHED("add_columns_kernel");
   return 0;
 }
@@ -732,7 +789,7 @@ int launch_gather_rows(float *dst, int64_t dst_stride, const float *src, int64_t
                        int count, int dim, cudaStream_t stream) {
   if (count <= 0) return 0;
   launch(gather_rows_kernel, blocks_for((int64_t)count * dim, 256), 256, 0, stream, dst, dst_stride, src, src_stride,
-                                                                                idx, count, dim);
+         idx, count, dim);
   B200_LAUNCHED("gather_rows_kernel");
   return 0;
 }
@@ -741,7 +798,7 @@ int launch_scales_by_group(float *dst, int64_t t_stride, const float *src, int64
                            cudaStream_t stream) {
   if (count <= 0 || groups <= 0) return 0;
   launch(scales_by_group_kernel, blocks_for((int64_t)count * groups, 256), 256, 0, stream, dst, t_stride, src, s_stride,
-                                                                                      count, groups);
+         count, groups);
   B200_LAUNCHED("scales_by_group_kernel");
   return 0;
 }
@@ -750,7 +807,7 @@ int launch_outlier_columns(float *cols, const int8_t *w, const float *s, int sst
                            const int32_t *channels, int nch, cudaStream_t stream) {
   if (nch <= 0) return 0;
   launch(outlier_columns_kernel, blocks_for((int64_t)vocab * nch, 256), 256, 0, stream, cols, w, s, sstride, dim, vocab,
-                                                                                     channels, nch);
+         channels, nch);
   B200_LAUNCHED("outlier_columns_kernel");
   return 0;
 }
@@ -790,7 +847,7 @@ int launch_advance(int32_t *tokens, int32_t *pos, const int32_t *ids, int32_t *h
   if (count <= 0) return 0;
   if (count > 1024) return fail(B200FWD_EINVAL, "advance: more than 1024 sequences");
   launch(advance_kernel, 1, ((count + 31) / 32) * 32, 0, stream, tokens, pos, ids, history, steps, step, count, logits,
-                                                             vocab, bad);
+         vocab, bad);
   B200_LAUNCHED("advance_kernel");
   return 0;
 }

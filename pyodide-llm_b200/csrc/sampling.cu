@@ -356,7 +356,7 @@ int launch_sample(int32_t *out, const float *logits, int64_t stride, int n, floa
   if (n < 1) return fail(B200FWD_EINVAL, "sample: no logits");
   if (!(temperature > 0)) return fail(B200FWD_EINVAL, "sample: the temperature must be above 0 (0 is greedy)");
   launch(sample_kernel, count, ST, 0, stream, out, logits, stride, n, temperature, topp, random, random0, rstride, step,
-                                          scratch, stacks, done);
+         scratch, stacks, done);
   B200_LAUNCHED("sample_kernel");
   return 0;
 }
@@ -367,8 +367,7 @@ int launch_advance_sampled(int32_t *tokens, int32_t *pos, const int32_t *ids, in
                            int32_t *made, int32_t *bad, cudaStream_t stream) {
   if (count > 1024) return fail(B200FWD_EINVAL, "sampled steps: at most 1024 sequences at once");
   launch(advance_sampled_kernel, 1, ((count + 31) / 32) * 32, 0, stream, tokens, pos, ids, history, steps, step, count,
-                                                                     logits, vocab, greedy, recent, window,
-                                                                     recent_count, stops, nstops, done, made, bad);
+         logits, vocab, greedy, recent, window, recent_count, stops, nstops, done, made, bad);
   B200_LAUNCHED("advance_sampled_kernel");
   return 0;
 }

@@ -853,7 +853,8 @@ template <int G>
 __global__ void __launch_bounds__(32)
     attn_values_decode_h(float *out, int64_t out_stride, const uint16_t *vc, const float *att, const int32_t *seq,
                          const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
-                         int h1, float one) {
+                         int h1, float one, int8_t *xq, int64_t q_stride, float *xs, int64_t s_stride,
+                         int64_t g_stride, int bias, int shift) {
   pdl_begin();
   __shared__ __align__(16) uint32_t vbuf[HNB][HCH][32];  // raw float16 pairs: [chunk][position][lane]
   __shared__ __align__(16) uint64_t wbuf[2][G][HCH];     // the weights x 2^112, twice: [chunk & 1][head][position]
@@ -944,6 +945,32 @@ __global__ void __launch_bounds__(32)
     float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + dim0 + 2 * lane;
     dst[0] = lo(o[g]);
     dst[1] = hi(o[g]);
+    if (xq) {
+      // quantize_x (kernel.ts:129-156) of the head's values dim0 .. + 63: two groups of 32, on lanes 0-15 and 16-31,
+      // value 2(l % 16) + e of its group on lane l. Class (index mod 4) 0 and 1 are the even lanes' two values, 2
+      // and 3 the odd lanes': each class's largest |value| over the eight lanes of its parity, then the scalar
+      // comparisons, scale and rounding of quantize_group.
+      float ma = fabsf(lo(o[g])), mb = fabsf(hi(o[g]));
+#pragma unroll
+      for (int x = 2; x <= 8; x <<= 1) {
+        ma = wmax(ma, __shfl_xor_sync(FULL, ma, x));
+        mb = wmax(mb, __shfl_xor_sync(FULL, mb, x));
+      }
+      const float oa = __shfl_xor_sync(FULL, ma, 1), ob = __shfl_xor_sync(FULL, mb, 1);
+      const bool even = (lane & 1) == 0;
+      float amax = even ? ma : oa;
+      const float m1 = even ? mb : ob, m2 = even ? oa : ma, m3 = even ? ob : mb;
+      if (m1 > amax) amax = m1;
+      if (m2 > amax) amax = m2;
+      if (m3 > amax) amax = m3;
+      const float scale = fdiv(amax, bias == 0 ? 127.0f : 63.0f);
+      const float inv = scale > 0 ? fdiv(1.0f, scale) : 0.0f;
+      const uint32_t q0 = (uint8_t)(int8_t)(quantize_one(lo(o[g]), inv, bias) - shift);
+      const uint32_t q1 = (uint8_t)(int8_t)(quantize_one(hi(o[g]), inv, bias) - shift);
+      const int64_t j = (int64_t)h * hs + dim0 + 2 * lane;
+      *reinterpret_cast<uint16_t *>(xq + (int64_t)tok * q_stride + j) = (uint16_t)(q0 | (q1 << 8));
+      if ((lane & 15) == 0) xs[(int64_t)tok * s_stride + (j >> 5) * g_stride] = scale;
+    }
   }
 }
 
@@ -966,7 +993,7 @@ template <bool HALF, int G>
 int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                  float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
                  int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1, int vec,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, AttentionQuant *quant) {
   const size_t smem_soft = (size_t)max_count * sizeof(float);
   if (smem_soft > MAX_SOFTMAX_SMEM) return fail(B200FWD_EINVAL, "attention: more positions than one block's shared memory");
   if (!tiles && vec && hs % 2 == 0 && G * (hs / 2) <= 1024) {
@@ -989,9 +1016,15 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
       return c == 1 || c == 2 || c == 4 || c == 8 ? c : 2;
     }();
     if (HALF && hs % 64 == 0) {
+      // every head written: quantize_x of the rows in the same kernel (2-byte stores of a lane's two values)
+      const bool fold = quant && h0 == 0 && h1 == nh && reinterpret_cast<uintptr_t>(quant->xq) % 2 == 0 &&
+                        quant->q_stride % 2 == 0;
       launch(attn_values_decode_h<G>, dim3(nkv * (hs / 64), count), 32, 0, stream, out, out_stride,
-             static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f);
+             static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f,
+             fold ? quant->xq : nullptr, fold ? quant->q_stride : 0, fold ? quant->xs : nullptr,
+             fold ? quant->s_stride : 0, fold ? quant->g_stride : 0, fold ? quant->bias : 0, fold ? quant->shift : 0);
       B200_LAUNCHED("attn_values_decode_h");
+      if (fold) quant->done = 1;
       return 0;
     }
     int parts = 1;
@@ -1073,7 +1106,8 @@ int prepare_attention() {
 int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                      float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
                      int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1,
-                     int half, cudaStream_t stream) {
+                     int half, cudaStream_t stream, AttentionQuant *quant) {
+  if (quant) quant->done = 0;
   if (count <= 0) return 0;
   if (nkv <= 0 || nh % nkv) return fail(B200FWD_EINVAL, "attention: heads must be a multiple of the kv heads");
   if (max_count > P) return fail(B200FWD_EINVAL, "attention: a position past the scratch");
@@ -1086,7 +1120,7 @@ int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_s
   const int G = nh / nkv;
 #define B200_ATT(H, GG)                                                                                            \
   return launch_tiled<H, GG>(out, out_stride, q, q_stride, kc, vc, att, seq, pos, pos0, tiles, ntiles, count,     \
-                             seq_stride, P, max_count, nh, nkv, hs, h0, h1, vec, stream)
+                             seq_stride, P, max_count, nh, nkv, hs, h0, h1, vec, stream, quant)
   if (half) {
     switch (G) {
       case 1: B200_ATT(true, 1);

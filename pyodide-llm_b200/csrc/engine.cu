@@ -381,10 +381,12 @@ int forward_device(b200fwd_engine *e, int n, int want, int max_count, int ntiles
     CHECK(launch_rope_cache(q, QKV, k, v, QKV, e->cosT, e->sinT, e->pos_d(), e->seq_d(), n, e->layer_keys(l),
                             e->layer_values(l), e->seq_stride(), e->half ? 1 : 0, e->heads, e->kvHeads, e->hs,
                             e->plan.rotary, st));
+    // the attention kernels quantize their rows themselves where they can (single tokens); else quantize_x after
+    AttentionQuant aq{e->xq, XQ, e->xs, 1, TP, e->bias, shift, 0};
     CHECK(launch_attention(e->xb, QD, q, QKV, e->layer_keys(l), e->layer_values(l), e->att, e->seq_d(), e->pos_d(), 0,
                            ntiles ? e->tiles_d() : nullptr, ntiles, n, e->seq_stride(), e->capacity, max_count,
-                           e->heads, e->kvHeads, e->hs, 0, e->heads, e->half ? 1 : 0, st));
-    CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, 1, TP, st, shift));
+                           e->heads, e->kvHeads, e->hs, 0, e->heads, e->half ? 1 : 0, st, &aq));
+    if (!aq.done) CHECK(launch_quantize(e->xb, QD, QD, e->bias, n, e->xq, XQ, e->xs, 1, TP, st, shift));
     CHECK(matmul(e, e->wo, l, e->x, D, 1, n));
     CHECK(launch_norm_quantize(e->x, D, e->ffnW + (int64_t)l * D, D, e->eps, e->bias, n, e->xq, XQ, e->xs, 1, TP,
                                nullptr, 0, nullptr, nullptr, 0, st, shift));

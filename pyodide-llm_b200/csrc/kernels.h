@@ -64,10 +64,20 @@ int launch_rope_cache(float *q, int64_t q_stride, const float *k, const float *v
 // (first token, count) of up to 16 consecutive tokens of one sequence at consecutive positions, sharing the keys and
 // values they read; null: every token its own tile. att: [count][nh][P] scratch (P >= max position + 1), left
 // holding the softmax weights; max_count bounds pos + 1 for the grid. Heads h0..h1.
+// quant (may be null): where the kernels may also write out's rows as quantize_x writes them (launch_quantize's
+// arguments); done = 1 when they did, so the caller's own quantize_x of out is not needed.
+struct AttentionQuant {
+  int8_t *xq;
+  int64_t q_stride;
+  float *xs;
+  int64_t s_stride, g_stride;
+  int bias, shift;
+  int done;
+};
 int launch_attention(float *out, int64_t out_stride, const float *q, int64_t q_stride, const void *kc, const void *vc,
                      float *att, const int32_t *seq, const int32_t *pos, int pos0, const int32_t *tiles, int ntiles,
                      int count, int64_t seq_stride, int P, int max_count, int nh, int nkv, int hs, int h0, int h1,
-                     int half, cudaStream_t stream);
+                     int half, cudaStream_t stream, AttentionQuant *quant = nullptr);
 constexpr int ATTN_TILE = 16;  // tokens of a tile at most
 // the attention kernels' shared-memory opt-in on the current device (once; before any graph capture)
 int prepare_attention();

@@ -337,9 +337,12 @@ def test_prompt_blocks_of_wide_heads(heads, kv_heads, half_keys):
     """Prompt blocks of heads of 64 values (the register-blocked prompt attention: 1, 2, 4 and 8 query heads per kv
     head): three sequences' prompts of ragged lengths, run in two calls of several sequences each, so that tiles of
     up to 16 tokens read keys and values past three 64-position chunks and the last tile of a run is short; each
-    sequence's last logits against the oracle's token-by-token forward, to the bit."""
+    sequence's last logits against the oracle's token-by-token forward, to the bit. Then four greedy steps of all
+    three on the device (the single-token attention kernels, which quantize their rows themselves): the ids, and the
+    second layer's keys and values at the new positions (they depend on the first layer's quantized attention rows),
+    to the bit."""
     dim = 64 * heads
-    header = (dim, 2 * dim, 1, heads, kv_heads, 320, 512)
+    header = (dim, 2 * dim, 2, heads, kv_heads, 320, 512)
     data = ck.synthetic_checkpoint(header, seed=heads * 10 + kv_heads, norm="normal")
     plan = ck.make_plan(header, lambda o, n: data[o:o + n])
     lengths = [150, 83, 211]
@@ -361,10 +364,20 @@ def test_prompt_blocks_of_wide_heads(heads, kv_heads, half_keys):
         ends = [s for s, w in zip(slots, want) if w]
         for s, row in zip(ends, logits):
             got[s] = row.copy()
+    steps = 4
+    first = np.array([int(np.argmax(got[s])) for s in range(3)], np.int32)
+    ids = eng.generate_greedy(np.arange(3, dtype=np.int32), first, np.array(lengths, np.int32), steps)
+    kv = [eng.keysAndValues(len(p), steps, slot=s) for s, p in enumerate(prompts)]
     eng.release()
     for s, p in enumerate(prompts):
         ref = oracle.OracleEngine(data, plan, half_keys=1 if half_keys else 0, threads=2)
         ref.forward_many([int(t) for t in p[:-1]], 0)
         want = ref.forward(int(p[-1]), len(p) - 1)
-        ref.close()
         assert np.array_equal(bits(got[s]), bits(want)), s
+        token = int(np.argmax(want))
+        for i in range(steps):
+            token = int(np.argmax(ref.forward(token, len(p) + i)))
+            assert token == ids[s, i], (s, i)
+        rk, rv = ref.keys_values(len(p), steps)
+        ref.close()
+        assert np.array_equal(bits(kv[s]["keys"]), bits(rk)) and np.array_equal(bits(kv[s]["values"]), bits(rv)), s

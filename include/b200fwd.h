@@ -208,6 +208,12 @@ int b200k_matmul_q8r(float *xout, const int8_t *xq, const float *xs, const int8_
 int b200k_matmul_q8s(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
                      int64_t ws_stride, int32_t n, int32_t rows, int32_t count, int64_t out_stride, int64_t q_stride,
                      int64_t s_stride, b200fwd_stream stream);
+/* No counterpart in the reference: the tensor-core matmul the engine launches for one rows x n matrix of its layers
+ * at count tokens (count >= 2) on a GPU of `sms` SMs, with token tiles of at most `widest` (16, 32 or 64): *lane_split
+ * 1 for q8_gemm_lanes (a cluster of four CTAs per tile, one per chain lane), 0 for q8_gemm_tc; *tile_tokens the
+ * tile's tokens. The choice of least estimated time from measured stage times; host arithmetic only (no device). */
+int b200k_matmul_plan(int32_t rows, int32_t n, int32_t count, int32_t sms, int32_t widest, int32_t *lane_split,
+                      int32_t *tile_tokens);
 /* kernel.ts:231-258 matmul_q8: the same on quantize_x(bias 0) activations, lane order of dot32. */
 int b200k_matmul_q8(float *xout, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int32_t n,
                     int32_t r0, int32_t r1, int32_t count, int64_t out_stride, int64_t q_stride, int64_t s_stride,

@@ -167,6 +167,7 @@ def load():
         "b200fwd_generate_many": (P, I32, P, P, P, I32, ctypes.c_float, ctypes.c_float, ctypes.c_float, P, P, P, P,
                                   I32, P, P),
         "b200k_attention_batch": (P, P, P, P, P, P, P, I32, I64, I32, I32, I32, I32, I32, P),
+        "b200k_matmul_plan": (I32, I32, I32, I32, I32, P, P),
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

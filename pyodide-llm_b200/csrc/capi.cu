@@ -174,6 +174,21 @@ int b200k_attention(float *out, const float *q, const void *kc, const void *vc, 
   });
 }
 
+int b200k_matmul_plan(int32_t rows, int32_t n, int32_t count, int32_t sms, int32_t widest, int32_t *lane_split,
+                      int32_t *tile_tokens) {
+  return guarded([&] {
+    if (rows < 1 || n < 32 || n % 32 || count < 2 || sms < 1 || !(widest == 16 || widest == 32 || widest == 64) ||
+        !lane_split || !tile_tokens)
+      return fail(B200FWD_EINVAL, "matmul_plan: bad arguments");
+    // the engine's rule (engine.cu matmul): the lane split where it fits and its estimate is the lower
+    const bool lanes = widest == 64 && gemm_lanes_enabled() && gemm_lanes_fits(n, rows, count) &&
+                       gemm_lanes_pays(rows, count, n, sms, widest);
+    *lane_split = lanes ? 1 : 0;
+    *tile_tokens = lanes ? choose_lanes_bn(count, widest) : choose_gemm_bn(rows, count, sms, widest);
+    return 0;
+  });
+}
+
 int b200k_attention_batch(float *out, const float *q, const void *kc, const void *vc, float *att, const int32_t *seq,
                           const int32_t *pos, int32_t n, int64_t seq_stride, int32_t scratch_positions, int32_t nh,
                           int32_t nkv, int32_t hs, int32_t half, b200fwd_stream stream) {

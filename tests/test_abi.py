@@ -87,3 +87,41 @@ def test_make_plan_8b_shape():
     weights = sum(np.prod(t["shape"]) for n, t in tensors.items() if t["kind"] == "int8")
     assert weights == 8_029_995_008  # layers 6.98e9 + embedding and classifier 0.525e9 each
     assert size == 28 + weights * 9 // 8 + 4 * (32 * 4096 * 2 + 4096)
+
+
+# the engine's matmul choices for the 8B projections on 148 SMs, as measured per launch (every layer's copy in turn):
+# (lane split, tile tokens) by token count, for q|k|v 6144x4096, o 4096x4096, w1|w3 28672x4096, w2 4096x14336 and the
+# classifier 128256x4096
+MATMUL_PLANS = {
+    2: [(1, 16), (1, 16), (0, 16), (1, 16), (0, 16)],
+    8: [(1, 16), (1, 16), (0, 16), (1, 16), (0, 16)],
+    32: [(1, 32), (1, 32), (0, 32), (1, 32), (0, 32)],
+    48: [(0, 16), (1, 64), (0, 64), (1, 64), (0, 64)],
+    64: [(1, 64), (1, 64), (0, 64), (1, 64), (0, 64)],
+    128: [(0, 64), (1, 64), (0, 64), (1, 64), (0, 64)],
+    512: [(0, 64), (0, 64), (0, 64), (0, 64), (0, 64)],
+}
+SHAPES_8B = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336), (128256, 4096)]
+
+
+@pytest.mark.parametrize("count", sorted(MATMUL_PLANS))
+def test_matmul_plan_of_the_8b_shapes(lib, count):
+    """b200k_matmul_plan: the kernel and tile width the engine takes per matrix, from the measured stage times (at 64
+    tokens, q|k|v, o and w2 on the lane split, w1|w3 and the classifier on one CTA a tile of 64 tokens)."""
+    lane, tile = ctypes.c_int32(), ctypes.c_int32()
+    got = []
+    for rows, n in SHAPES_8B:
+        assert lib.b200k_matmul_plan(rows, n, count, 148, 64, ctypes.byref(lane), ctypes.byref(tile)) == 0
+        got.append((lane.value, tile.value))
+    assert got == MATMUL_PLANS[count]
+
+
+def test_matmul_plan_refusals(lib):
+    lane, tile = ctypes.c_int32(), ctypes.c_int32()
+    assert lib.b200k_matmul_plan(4096, 4096, 1, 148, 64, ctypes.byref(lane), ctypes.byref(tile)) == abi.EINVAL
+    assert lib.b200k_matmul_plan(4096, 100, 64, 148, 64, ctypes.byref(lane), ctypes.byref(tile)) == abi.EINVAL
+    assert lib.b200k_matmul_plan(4096, 4096, 64, 148, 48, ctypes.byref(lane), ctypes.byref(tile)) == abi.EINVAL
+    # tiles of at most 32 tokens (activations of fewer than 64 tokens): no lane split; o's 32 row tiles x four
+    # 16-token tiles still fit the SMs in one round, and a 16-token stage is the cheaper (23.2 against 27.7 us)
+    assert lib.b200k_matmul_plan(4096, 4096, 64, 148, 32, ctypes.byref(lane), ctypes.byref(tile)) == 0
+    assert (lane.value, tile.value) == (0, 16)

@@ -849,7 +849,8 @@ __device__ __forceinline__ uint64_t half2_bits(uint32_t u) {
 // one by one (kernel.ts:522-565). The values come in chunks of HCH positions by cp.async, HNB - 1 chunks ahead; the
 // chunk's weights (times 2^112, each twice for the paired multiplies) are read one chunk ahead into registers and
 // stored to shared memory after the chunk before is done.
-template <int G>
+// QUANT: also write the rows quantized (xq, xs); the instance without it keeps the registers of the sums alone.
+template <int G, bool QUANT>
 __global__ void __launch_bounds__(32)
     attn_values_decode_h(float *out, int64_t out_stride, const uint16_t *vc, const float *att, const int32_t *seq,
                          const int32_t *pos, int pos0, int64_t seq_stride, int P, int nh, int nkv, int hs, int h0,
@@ -945,7 +946,7 @@ __global__ void __launch_bounds__(32)
     float *dst = out + (int64_t)tok * out_stride + (int64_t)h * hs + dim0 + 2 * lane;
     dst[0] = lo(o[g]);
     dst[1] = hi(o[g]);
-    if (xq) {
+    if (QUANT) {
       // quantize_x (kernel.ts:129-156) of the head's values dim0 .. + 63: two groups of 32, on lanes 0-15 and 16-31,
       // value 2(l % 16) + e of its group on lane l. Class (index mod 4) 0 and 1 are the even lanes' two values, 2
       // and 3 the odd lanes': each class's largest |value| over the eight lanes of its parity, then the scalar
@@ -1019,10 +1020,14 @@ int launch_tiled(float *out, int64_t out_stride, const float *q, int64_t q_strid
       // every head written: quantize_x of the rows in the same kernel (2-byte stores of a lane's two values)
       const bool fold = quant && h0 == 0 && h1 == nh && reinterpret_cast<uintptr_t>(quant->xq) % 2 == 0 &&
                         quant->q_stride % 2 == 0;
-      launch(attn_values_decode_h<G>, dim3(nkv * (hs / 64), count), 32, 0, stream, out, out_stride,
-             static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f,
-             fold ? quant->xq : nullptr, fold ? quant->q_stride : 0, fold ? quant->xs : nullptr,
-             fold ? quant->s_stride : 0, fold ? quant->g_stride : 0, fold ? quant->bias : 0, fold ? quant->shift : 0);
+      if (fold)
+        launch(attn_values_decode_h<G, true>, dim3(nkv * (hs / 64), count), 32, 0, stream, out, out_stride,
+               static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f,
+               quant->xq, quant->q_stride, quant->xs, quant->s_stride, quant->g_stride, quant->bias, quant->shift);
+      else
+        launch(attn_values_decode_h<G, false>, dim3(nkv * (hs / 64), count), 32, 0, stream, out, out_stride,
+               static_cast<const uint16_t *>(vc), att, seq, pos, pos0, seq_stride, P, nh, nkv, hs, h0, h1, 1.0f,
+               nullptr, 0, nullptr, 0, 0, 0, 0);
       B200_LAUNCHED("attn_values_decode_h");
       if (fold) quant->done = 1;
       return 0;
